@@ -1,0 +1,149 @@
+/*
+ * pla_b200.h — C ABI of the B200 (sm_100a) 7x7 depthwise-convolution and
+ * 7x7 stencil library.
+ *
+ * Every entry point takes plain device pointers, element counts/strides and a
+ * CUDA stream, launches asynchronously on that stream and returns a status
+ * code (PLA_OK == 0).  Nothing here allocates device memory, synchronises the
+ * stream or falls back to a CPU path: a non-zero status means no kernel ran.
+ *
+ * Numerical contract (shared by every kernel and by the CPU oracle that the
+ * tests check against): each output point is
+ *
+ *     acc = 0;  for ky in 0..6: for kx in 0..6:
+ *                   acc = fma(x[i+ky-3][j+kx-3], w[ky][kx], acc)
+ *     y[i][j] = round_to_output_dtype(acc + bias)      (bias add skipped if null)
+ *
+ * with x == 0 outside the plane (zero padding 3, cross-correlation, output size
+ * == input size), the accumulator in fp32 for fp32/bf16/fp16 data and fp64 for
+ * fp64 data.  This is the semantics of torch.nn.Conv2d(C, C, 7, stride=1,
+ * padding=3, groups=C) used by the reference modules, evaluated in one fixed
+ * tap order so that results are bit-reproducible.
+ */
+#ifndef PLA_B200_H_
+#define PLA_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define PLA_API __attribute__((visibility("default")))
+#else
+#define PLA_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Opaque CUDA stream handle (binary-compatible with cudaStream_t). */
+typedef struct CUstream_st* pla_stream_t;
+
+/* Element type codes.  The values are the ones the reference stencil launcher
+ * uses for its `type` argument (data/stencil_direct_cuda_v7/stencil_cuda.cpp:30:
+ * 0=float16, 1=float32, 2=float64, 3=bfloat16). */
+enum pla_dtype {
+  PLA_F16 = 0,
+  PLA_F32 = 1,
+  PLA_F64 = 2,
+  PLA_BF16 = 3
+};
+
+/* Memory layout of a depthwise activation tensor [N, C, H, W]. */
+enum pla_layout {
+  PLA_NCHW = 0, /* torch.contiguous_format */
+  PLA_NHWC = 1  /* torch.channels_last */
+};
+
+/* Status codes. */
+enum pla_status {
+  PLA_OK = 0,
+  PLA_ERR_INVALID_ARGUMENT = 1, /* null pointer, negative size, bad enum   */
+  PLA_ERR_UNSUPPORTED = 2,      /* dtype/layout/shape outside this library */
+  PLA_ERR_TOO_LARGE = 3,        /* size exceeds grid/indexing limits       */
+  PLA_ERR_CUDA = 4,             /* a CUDA runtime/driver call failed       */
+  PLA_ERR_NO_DEVICE = 5,        /* no sm_100 device current                */
+  PLA_ERR_DEVICE_FAULT = 6      /* a kernel recorded a bounded-wait timeout */
+};
+
+/* Human-readable text for a status code (static storage, never NULL). */
+PLA_API const char* pla_status_string(int status);
+
+/* The last CUDA error text seen by this thread inside the library. */
+PLA_API const char* pla_last_cuda_error(void);
+
+/* Library ABI version: (major << 16) | minor. */
+PLA_API int pla_version(void);
+
+/*
+ * Single-step 7x7 stencil, one filter for all planes:
+ *     y[n,0,:,:] = stencil(x[n,0,:,:]; w[0..48]) + b[0]
+ *
+ * Replaces the reference launchers
+ *   launch_direct()  data/stencil_direct_cuda_v7/stencil_cuda_kernel.cu:230-244
+ *   launch_stencil() data/stencil_cuda_v2/stencil_cuda_kernel.cu:195-209
+ * with the argument meaning of launch_direct: x may be strided
+ * (element strides sn, sh, sw; sn ignored when n == 1), y is contiguous
+ * [n, h, width], w holds 49 taps row-major, b is NULL or one element, all of
+ * dtype `dtype` (enum pla_dtype).  Unlike the reference it returns a status.
+ */
+PLA_API int pla_stencil7x7_forward(const void* x, const void* w, const void* b, void* y,
+                           int n, int h, int width,
+                           int64_t sn, int64_t sh, int64_t sw,
+                           int dtype, pla_stream_t stream);
+
+/*
+ * Depthwise 7x7 convolution (groups = C, stride 1, padding 3):
+ *     y[n,c] = stencil(x[n,c]; w[c, 0..48]) + b[c]
+ *
+ * Replaces launch_depthwise_7x7_cutlass()
+ *   data/depthwise_conv_7x7_cuda/model_cutlass_autotune_v6.py:428-458
+ *   (and the v1/v5 launchers, model_cutlass.py:263-279,
+ *    model_cutlass_autotune_v5.py:403-420).
+ * Differences: w is the module's own [C,1,7,7] weight (no [C,8,80] repack),
+ * b may be non-NULL ([C]), dtype may be f32/bf16/f16/f64 and layout NCHW or
+ * NHWC.  x and y are dense in `layout`.
+ */
+PLA_API int pla_depthwise7x7_forward(const void* x, const void* w, const void* b, void* y,
+                             int n, int c, int h, int width,
+                             int dtype, int layout, pla_stream_t stream);
+
+/*
+ * Iterated stencil on one device (no reference counterpart; the reference
+ * path is data/stencil_7x7.py:10-12 applied `steps` times with zero padding
+ * each step, i.e. a zero Dirichlet boundary):
+ *     u_0 = x;  u_{t+1} = stencil(u_t; w) (+ b if non-NULL);  y = u_steps
+ * fp32/bf16/f16 planes [h, width], contiguous.  `scratch` is a caller-owned
+ * device buffer of at least h*width elements used as the second ping-pong
+ * buffer; x is only read; y may alias x.
+ */
+PLA_API int pla_stencil7x7_iterate(const void* x, const void* w, const void* b, void* y,
+                           void* scratch, int h, int width, int steps,
+                           int dtype, pla_stream_t stream);
+
+/*
+ * One Jacobi step of a row band of a larger grid (building block of the
+ * row-band multi-GPU iterated stencil; no reference counterpart).
+ * `in` and `out` are band buffers of (rows + 6) x width elements: rows 0..2
+ * hold the 3 halo rows above the band, rows 3..rows+2 the band itself and
+ * rows rows+3..rows+5 the halo rows below it.  The step writes output band
+ * rows [row_begin, row_end) (0 <= row_begin <= row_end <= rows) into
+ * out rows 3+row_begin .. 3+row_end-1; halo rows of `out` are not touched.
+ */
+PLA_API int pla_stencil7x7_band_step(const void* in, const void* w, const void* b, void* out,
+                             int rows, int width, int row_begin, int row_end,
+                             int dtype, pla_stream_t stream);
+
+/*
+ * Device-side fault word of the current device: bit 0 = an mbarrier wait in a
+ * kernel gave up after its iteration bound.  Reading it synchronises the
+ * device.  pla_clear_device_faults() zeroes it.
+ */
+PLA_API int pla_read_device_faults(unsigned int* faults);
+PLA_API int pla_clear_device_faults(void);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* PLA_B200_H_ */

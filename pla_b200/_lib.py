@@ -1,0 +1,78 @@
+"""ctypes binding of libpla_b200.so (the C ABI declared in include/pla_b200.h).
+
+The shared library is built in-tree (``python -m pla_b200.build``); importing
+the ops without it, or calling them on a non-CUDA tensor, raises: there is no
+CPU or eager-PyTorch fallback anywhere in this package.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import torch
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libpla_b200.so")
+
+PLA_F16, PLA_F32, PLA_F64, PLA_BF16 = 0, 1, 2, 3
+PLA_NCHW, PLA_NHWC = 0, 1
+
+DTYPE_CODE = {
+    torch.float16: PLA_F16,
+    torch.float32: PLA_F32,
+    torch.float64: PLA_F64,
+    torch.bfloat16: PLA_BF16,
+}
+
+# Every symbol include/pla_b200.h declares, with its ctypes signature.
+_vp, _i32, _i64, _u32p = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.POINTER(ctypes.c_uint)
+SIGNATURES = {
+    "pla_status_string": ([_i32], ctypes.c_char_p),
+    "pla_last_cuda_error": ([], ctypes.c_char_p),
+    "pla_version": ([], _i32),
+    "pla_stencil7x7_forward": ([_vp, _vp, _vp, _vp, _i32, _i32, _i32, _i64, _i64, _i64, _i32, _vp], _i32),
+    "pla_depthwise7x7_forward": ([_vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _i32, _vp], _i32),
+    "pla_stencil7x7_iterate": ([_vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _vp], _i32),
+    "pla_stencil7x7_band_step": ([_vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _vp], _i32),
+    "pla_read_device_faults": ([_u32p], _i32),
+    "pla_clear_device_faults": ([], _i32),
+}
+
+_lib = None
+
+
+class PlaError(RuntimeError):
+    """A non-zero status from the C ABI (mirrors the reference's TORCH_CHECK -> RuntimeError)."""
+
+
+def lib() -> ctypes.CDLL:
+    """Load libpla_b200.so once; raise if it has not been built."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(
+                f"{LIB_PATH} is missing: build the CUDA library first (python -m pla_b200.build); "
+                "this package has no CPU fallback")
+        handle = ctypes.CDLL(LIB_PATH)
+        for name, (argtypes, restype) in SIGNATURES.items():
+            fn = getattr(handle, name)
+            fn.argtypes = argtypes
+            fn.restype = restype
+        _lib = handle
+    return _lib
+
+
+def check(status: int, what: str) -> None:
+    if status != 0:
+        L = lib()
+        msg = L.pla_status_string(status).decode()
+        detail = L.pla_last_cuda_error().decode()
+        raise PlaError(f"{what}: {msg}" + (f" ({detail})" if detail and status == 4 else ""))
+
+
+def stream_ptr(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def ptr(t: torch.Tensor | None):
+    return None if t is None else t.data_ptr()

@@ -1,0 +1,438 @@
+// C ABI of the library (declarations and contract: include/pla_b200.h).
+//
+// Host-side dispatch: validates arguments, picks the kernel family, builds the
+// TMA tensor map and launches on the caller's stream.  No allocation, no
+// synchronisation, no CPU fallback.
+#include <cudaTypedefs.h>
+
+#include <atomic>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "../../include/pla_b200.h"
+#include "cm_kernel.cuh"
+#include "generic_kernel.cuh"
+#include "pla_common.cuh"
+#include "tile_kernel.cuh"
+
+namespace pla {
+namespace {
+
+thread_local char g_last_cuda_error[256] = "";
+
+int cuda_fail(cudaError_t e, const char* where) {
+  std::snprintf(g_last_cuda_error, sizeof(g_last_cuda_error), "%s: %s", where, cudaGetErrorString(e));
+  return PLA_ERR_CUDA;
+}
+
+#define PLA_CUDA(call)                              \
+  do {                                              \
+    cudaError_t e_ = (call);                        \
+    if (e_ != cudaSuccess) return cuda_fail(e_, #call); \
+  } while (0)
+
+constexpr int kMaxDevices = 64;
+
+struct DeviceInfo {
+  std::once_flag once;
+  int status = PLA_OK;
+  int sms = 0;
+  int cc_major = 0;
+  size_t smem_optin = 0;
+};
+DeviceInfo g_dev[kMaxDevices];
+
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+
+int current_device(int* dev) {
+  cudaError_t e = cudaGetDevice(dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (*dev < 0 || *dev >= kMaxDevices) return PLA_ERR_NO_DEVICE;
+  return PLA_OK;
+}
+
+DeviceInfo* device_info(int* status) {
+  int dev;
+  *status = current_device(&dev);
+  if (*status != PLA_OK) return nullptr;
+  DeviceInfo& d = g_dev[dev];
+  std::call_once(d.once, [&]() {
+    cudaDeviceProp p;
+    cudaError_t e = cudaGetDeviceProperties(&p, dev);
+    if (e != cudaSuccess) {
+      d.status = cuda_fail(e, "cudaGetDeviceProperties");
+      return;
+    }
+    d.sms = p.multiProcessorCount;
+    d.cc_major = p.major;
+    d.smem_optin = p.sharedMemPerBlockOptin;
+    if (p.major != 10) d.status = PLA_ERR_NO_DEVICE;
+  });
+  *status = d.status;
+  return d.status == PLA_OK ? &d : nullptr;
+}
+
+int encoder(PFN_cuTensorMapEncodeTiled_v12000* fn) {
+  std::call_once(g_encode_once, []() {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  *fn = g_encode;
+  if (!g_encode) {
+    std::snprintf(g_last_cuda_error, sizeof(g_last_cuda_error), "cuTensorMapEncodeTiled unavailable");
+    return PLA_ERR_CUDA;
+  }
+  return PLA_OK;
+}
+
+size_t dtype_size(int dtype) {
+  switch (dtype) {
+    case PLA_F16: return 2;
+    case PLA_BF16: return 2;
+    case PLA_F32: return 4;
+    case PLA_F64: return 8;
+    default: return 0;
+  }
+}
+
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+// Per-(kernel, device) one-time attribute setup (dynamic smem opt-in) and
+// the resident-CTA count used to size persistent grids.
+template <auto Kernel>
+int kernel_setup(int threads, uint32_t smem, int* blocks_per_sm) {
+  int dev;
+  int st = current_device(&dev);
+  if (st != PLA_OK) return st;
+  static std::mutex mu;
+  static std::atomic<int> cached[kMaxDevices] = {};
+  int v = cached[dev].load(std::memory_order_acquire);
+  if (v == 0) {
+    std::lock_guard<std::mutex> lock(mu);
+    v = cached[dev].load(std::memory_order_relaxed);
+    if (v == 0) {
+      PLA_CUDA(cudaFuncSetAttribute(Kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+      int nb = 0;
+      PLA_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, Kernel, threads, smem));
+      v = nb > 0 ? nb : 1;
+      cached[dev].store(v, std::memory_order_release);
+    }
+  }
+  *blocks_per_sm = v;
+  return PLA_OK;
+}
+
+CUtensorMapDataType tmap_dtype(int dtype) {
+  switch (dtype) {
+    case PLA_F16: return CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    case PLA_BF16: return CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    default: return CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+  }
+}
+
+// Stack of `planes` planes of `rows` x `width` elements; strides in elements.
+template <typename T, int R>
+int make_tile_map(CUtensorMap* map, const void* x, int dtype, int width, int rows, int planes,
+                  long long row_stride, long long plane_stride) {
+  using G = TileGeom<T, R>;
+  PFN_cuTensorMapEncodeTiled_v12000 enc;
+  int st = encoder(&enc);
+  if (st != PLA_OK) return st;
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(width), static_cast<cuuint64_t>(rows),
+                              static_cast<cuuint64_t>(planes)};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(row_stride) * sizeof(T),
+                                 static_cast<cuuint64_t>(plane_stride) * sizeof(T)};
+  const cuuint32_t box[3] = {static_cast<cuuint32_t>(G::PITCH), static_cast<cuuint32_t>(G::ROWS), 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(map, tmap_dtype(dtype), 3, const_cast<void*>(x), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    std::snprintf(g_last_cuda_error, sizeof(g_last_cuda_error), "cuTensorMapEncodeTiled failed (%d)",
+                  static_cast<int>(r));
+    return PLA_ERR_CUDA;
+  }
+  return PLA_OK;
+}
+
+constexpr int kTileR = 8;
+
+// Can the plane-tile kernel read this stack with TMA?
+bool tile_path_ok(const void* x, const void* y, int dtype, int width, long long row_stride,
+                  long long plane_stride, int planes) {
+  if (dtype != PLA_F32 && dtype != PLA_BF16 && dtype != PLA_F16) return false;
+  const size_t es = dtype_size(dtype);
+  if (!aligned(x, 16) || !aligned(y, 16)) return false;
+  if (width % 4 != 0) return false;                        // 4-wide vector stores
+  if ((row_stride * es) % 16 != 0) return false;           // TMA stride rule
+  if (planes > 1 && (plane_stride * es) % 16 != 0) return false;
+  if (row_stride * es >= (1ll << 40) || plane_stride * es >= (1ll << 40)) return false;
+  return true;
+}
+
+template <typename T>
+int launch_tile(const void* x, const void* w, const void* b, void* y, int dtype, int planes, int C, int in_rows,
+                int width, long long x_row_stride, long long x_plane_stride, int row_begin, int row_end,
+                int in_row_shift, long long y_plane_stride, long long y_row_stride, cudaStream_t stream) {
+  using G = TileGeom<T, kTileR>;
+  int st;
+  DeviceInfo* d = device_info(&st);
+  if (!d) return st;
+  if (row_end <= row_begin || planes == 0 || width == 0) return PLA_OK;
+  CUtensorMap map;
+  st = make_tile_map<T, kTileR>(&map, x, dtype, width, in_rows, planes, x_row_stride, x_plane_stride);
+  if (st != PLA_OK) return st;
+  int per_sm = 1;
+  st = kernel_setup<tile_kernel<T, kTileR>>(kTileThreads, G::SMEM, &per_sm);
+  if (st != PLA_OK) return st;
+  TileArgs a;
+  a.w = w;
+  a.b = b;
+  a.y = y;
+  a.planes = planes;
+  a.C = C;
+  a.W = width;
+  a.row_begin = row_begin;
+  a.row_end = row_end;
+  a.in_row_shift = in_row_shift;
+  a.tiles_x = (width + kTileW - 1) / kTileW;
+  a.tiles_y = (row_end - row_begin + G::TH - 1) / G::TH;
+  a.total_tiles = static_cast<long long>(planes) * a.tiles_x * a.tiles_y;
+  a.y_plane_stride = y_plane_stride;
+  a.y_row_stride = y_row_stride;
+  const long long slots = static_cast<long long>(d->sms) * per_sm;
+  const int grid = static_cast<int>(a.total_tiles < slots ? a.total_tiles : slots);
+  tile_kernel<T, kTileR><<<grid, kTileThreads, G::SMEM, stream>>>(map, a);
+  PLA_CUDA(cudaGetLastError());
+  return PLA_OK;
+}
+
+int launch_tile_dtype(int dtype, const void* x, const void* w, const void* b, void* y, int planes, int C,
+                      int in_rows, int width, long long x_row_stride, long long x_plane_stride, int row_begin,
+                      int row_end, int in_row_shift, long long y_plane_stride, long long y_row_stride,
+                      cudaStream_t stream) {
+  switch (dtype) {
+    case PLA_F32:
+      return launch_tile<float>(x, w, b, y, dtype, planes, C, in_rows, width, x_row_stride, x_plane_stride,
+                                row_begin, row_end, in_row_shift, y_plane_stride, y_row_stride, stream);
+    case PLA_BF16:
+      return launch_tile<__nv_bfloat16>(x, w, b, y, dtype, planes, C, in_rows, width, x_row_stride,
+                                        x_plane_stride, row_begin, row_end, in_row_shift, y_plane_stride,
+                                        y_row_stride, stream);
+    case PLA_F16:
+      return launch_tile<__half>(x, w, b, y, dtype, planes, C, in_rows, width, x_row_stride, x_plane_stride,
+                                 row_begin, row_end, in_row_shift, y_plane_stride, y_row_stride, stream);
+    default:
+      return PLA_ERR_UNSUPPORTED;
+  }
+}
+
+template <typename T>
+int launch_generic(const GenericArgs& a, cudaStream_t stream) {
+  int st;
+  DeviceInfo* d = device_info(&st);
+  if (!d) return st;
+  if (a.total == 0) return PLA_OK;
+  long long blocks = (a.total + 255) / 256;
+  const long long cap = static_cast<long long>(d->sms) * 16;
+  if (blocks > cap) blocks = cap;
+  generic_kernel<T><<<static_cast<int>(blocks), 256, 0, stream>>>(a);
+  PLA_CUDA(cudaGetLastError());
+  return PLA_OK;
+}
+
+int launch_generic_dtype(int dtype, const GenericArgs& a, cudaStream_t stream) {
+  switch (dtype) {
+    case PLA_F32: return launch_generic<float>(a, stream);
+    case PLA_BF16: return launch_generic<__nv_bfloat16>(a, stream);
+    case PLA_F16: return launch_generic<__half>(a, stream);
+    case PLA_F64: return launch_generic<double>(a, stream);
+    default: return PLA_ERR_UNSUPPORTED;
+  }
+}
+
+template <typename T, bool NHWC, int BT>
+int launch_cm(const CmArgs& in, cudaStream_t stream) {
+  using G = CmGeom<BT>;
+  int st;
+  DeviceInfo* d = device_info(&st);
+  if (!d) return st;
+  int per_sm;
+  st = kernel_setup<cm_kernel<T, NHWC, BT>>(G::THREADS, G::SMEM, &per_sm);
+  if (st != PLA_OK) return st;
+  CmArgs a = in;
+  a.tiles_x = (a.W + G::TS - 1) / G::TS;
+  a.tiles_y = (a.H + G::TS - 1) / G::TS;
+  a.cgroups = (a.C + 31) / 32;
+  const long long NC = static_cast<long long>(a.N) * a.C;
+  a.groups = NHWC ? static_cast<long long>(a.N) * a.cgroups : (NC + 31) / 32;
+  const long long blocks = a.groups * a.tiles_x * a.tiles_y;
+  if (blocks == 0) return PLA_OK;
+  if (blocks > 0x7fffffffll) return PLA_ERR_TOO_LARGE;
+  cm_kernel<T, NHWC, BT><<<static_cast<int>(blocks), G::THREADS, G::SMEM, stream>>>(a);
+  PLA_CUDA(cudaGetLastError());
+  return PLA_OK;
+}
+
+template <typename T, bool NHWC>
+int launch_cm_bt(const CmArgs& a, cudaStream_t stream) {
+  if (a.H <= 7 && a.W <= 7) return launch_cm<T, NHWC, 1>(a, stream);
+  return launch_cm<T, NHWC, 2>(a, stream);
+}
+
+int launch_cm_dtype(int dtype, bool nhwc, const CmArgs& a, cudaStream_t stream) {
+  switch (dtype) {
+    case PLA_F32: return nhwc ? launch_cm_bt<float, true>(a, stream) : launch_cm_bt<float, false>(a, stream);
+    case PLA_BF16:
+      return nhwc ? launch_cm_bt<__nv_bfloat16, true>(a, stream) : launch_cm_bt<__nv_bfloat16, false>(a, stream);
+    case PLA_F16: return nhwc ? launch_cm_bt<__half, true>(a, stream) : launch_cm_bt<__half, false>(a, stream);
+    default: return PLA_ERR_UNSUPPORTED;
+  }
+}
+
+bool valid_dtype(int dtype) { return dtype_size(dtype) != 0; }
+
+}  // namespace
+}  // namespace pla
+
+using namespace pla;
+
+extern "C" {
+
+const char* pla_status_string(int status) {
+  switch (status) {
+    case PLA_OK: return "ok";
+    case PLA_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case PLA_ERR_UNSUPPORTED: return "unsupported dtype, layout or shape";
+    case PLA_ERR_TOO_LARGE: return "size exceeds supported limits";
+    case PLA_ERR_CUDA: return "CUDA error";
+    case PLA_ERR_NO_DEVICE: return "no sm_100 device is current";
+    case PLA_ERR_DEVICE_FAULT: return "a kernel recorded a device-side fault";
+    default: return "unknown status";
+  }
+}
+
+const char* pla_last_cuda_error(void) { return g_last_cuda_error; }
+
+int pla_version(void) { return (1 << 16) | 0; }
+
+int pla_stencil7x7_forward(const void* x, const void* w, const void* b, void* y, int n, int h, int width,
+                           int64_t sn, int64_t sh, int64_t sw, int dtype, pla_stream_t stream) {
+  if (!valid_dtype(dtype)) return PLA_ERR_UNSUPPORTED;
+  if (n < 0 || h < 0 || width < 0) return PLA_ERR_INVALID_ARGUMENT;
+  if (static_cast<long long>(n) * h * width == 0) return PLA_OK;
+  if (!x || !w || !y) return PLA_ERR_INVALID_ARGUMENT;
+  if (n > 65535 * 1024 || h > (1 << 30) || width > (1 << 30)) return PLA_ERR_TOO_LARGE;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const long long plane = static_cast<long long>(h) * width;
+  if (n == 1) sn = plane;  // ignored for a single plane
+  if (sw == 1 && tile_path_ok(x, y, dtype, width, sh, sn, n)) {
+    return launch_tile_dtype(dtype, x, w, b, y, n, 1, h, width, sh, sn, 0, h, 0, plane, width, s);
+  }
+  GenericArgs a;
+  a.x = x; a.w = w; a.b = b; a.y = y;
+  a.N = n; a.C = 1; a.H = h; a.W = width;
+  a.xs_n = sn; a.xs_c = 0; a.xs_h = sh; a.xs_w = sw;
+  a.ys_n = plane; a.ys_c = 0; a.ys_h = width; a.ys_w = 1;
+  a.total = static_cast<long long>(n) * plane;
+  return launch_generic_dtype(dtype, a, s);
+}
+
+int pla_depthwise7x7_forward(const void* x, const void* w, const void* b, void* y, int n, int c, int h,
+                             int width, int dtype, int layout, pla_stream_t stream) {
+  if (!valid_dtype(dtype)) return PLA_ERR_UNSUPPORTED;
+  if (layout != PLA_NCHW && layout != PLA_NHWC) return PLA_ERR_INVALID_ARGUMENT;
+  if (n < 0 || c < 0 || h < 0 || width < 0) return PLA_ERR_INVALID_ARGUMENT;
+  if (static_cast<long long>(n) * c * h * width == 0) return PLA_OK;
+  if (!x || !w || !y) return PLA_ERR_INVALID_ARGUMENT;
+  if (h > (1 << 30) || width > (1 << 30)) return PLA_ERR_TOO_LARGE;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const long long plane = static_cast<long long>(h) * width;
+  const long long planes = static_cast<long long>(n) * c;
+  if (dtype != PLA_F64) {
+    if (layout == PLA_NCHW && width >= 64 && planes <= 0x7fffffffll &&
+        tile_path_ok(x, y, dtype, width, width, plane, static_cast<int>(planes))) {
+      return launch_tile_dtype(dtype, x, w, b, y, static_cast<int>(planes), c, h, width, width, plane, 0, h, 0,
+                               plane, width, s);
+    }
+    CmArgs a;
+    a.x = x; a.w = w; a.b = b; a.y = y;
+    a.N = n; a.C = c; a.H = h; a.W = width;
+    return launch_cm_dtype(dtype, layout == PLA_NHWC, a, s);
+  }
+  GenericArgs a;
+  a.x = x; a.w = w; a.b = b; a.y = y;
+  a.N = n; a.C = c; a.H = h; a.W = width;
+  if (layout == PLA_NCHW) {
+    a.xs_n = c * plane; a.xs_c = plane; a.xs_h = width; a.xs_w = 1;
+  } else {
+    a.xs_n = c * plane; a.xs_c = 1; a.xs_h = static_cast<long long>(width) * c; a.xs_w = c;
+  }
+  a.ys_n = a.xs_n; a.ys_c = a.xs_c; a.ys_h = a.xs_h; a.ys_w = a.xs_w;
+  a.total = planes * plane;
+  return launch_generic_dtype(dtype, a, s);
+}
+
+int pla_stencil7x7_band_step(const void* in, const void* w, const void* b, void* out, int rows, int width,
+                             int row_begin, int row_end, int dtype, pla_stream_t stream) {
+  if (dtype != PLA_F32 && dtype != PLA_BF16 && dtype != PLA_F16) return PLA_ERR_UNSUPPORTED;
+  if (rows < 0 || width < 0 || row_begin < 0 || row_end < row_begin || row_end > rows)
+    return PLA_ERR_INVALID_ARGUMENT;
+  if (row_end == row_begin || width == 0) return PLA_OK;
+  if (!in || !w || !out) return PLA_ERR_INVALID_ARGUMENT;
+  const size_t es = dtype_size(dtype);
+  const long long band = static_cast<long long>(rows + 6) * width;
+  void* out_rows = static_cast<char*>(out) + 3ll * width * es;
+  if (!tile_path_ok(in, out_rows, dtype, width, width, band, 1)) return PLA_ERR_UNSUPPORTED;
+  return launch_tile_dtype(dtype, in, w, b, out_rows, 1, 1, rows + 6, width, width, band, row_begin, row_end, 3,
+                           band, width, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int pla_stencil7x7_iterate(const void* x, const void* w, const void* b, void* y, void* scratch, int h, int width,
+                           int steps, int dtype, pla_stream_t stream) {
+  if (dtype != PLA_F32 && dtype != PLA_BF16 && dtype != PLA_F16) return PLA_ERR_UNSUPPORTED;
+  if (h < 0 || width < 0 || steps < 0) return PLA_ERR_INVALID_ARGUMENT;
+  const long long plane = static_cast<long long>(h) * width;
+  if (plane == 0) return PLA_OK;
+  if (!x || !w || !y || (!scratch && steps > 0)) return PLA_ERR_INVALID_ARGUMENT;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const size_t bytes = static_cast<size_t>(plane) * dtype_size(dtype);
+  if (steps == 0) {
+    if (x != y) PLA_CUDA(cudaMemcpyAsync(y, x, bytes, cudaMemcpyDeviceToDevice, s));
+    return PLA_OK;
+  }
+  if (!tile_path_ok(x, y, dtype, width, width, plane, 1) || !aligned(scratch, 16)) return PLA_ERR_UNSUPPORTED;
+  const void* src = x;
+  if (x == y && (steps & 1)) {
+    // The first step would write into its own input: start from a copy.
+    PLA_CUDA(cudaMemcpyAsync(scratch, x, bytes, cudaMemcpyDeviceToDevice, s));
+    src = scratch;
+  }
+  for (int t = 0; t < steps; ++t) {
+    void* dst = ((steps - t) & 1) ? y : scratch;
+    int st = launch_tile_dtype(dtype, src, w, b, dst, 1, 1, h, width, width, plane, 0, h, 0, plane, width, s);
+    if (st != PLA_OK) return st;
+    src = dst;
+  }
+  return PLA_OK;
+}
+
+int pla_read_device_faults(unsigned int* faults) {
+  if (!faults) return PLA_ERR_INVALID_ARGUMENT;
+  PLA_CUDA(cudaMemcpyFromSymbol(faults, g_device_faults, sizeof(unsigned int)));
+  return PLA_OK;
+}
+
+int pla_clear_device_faults(void) {
+  const unsigned int zero = 0;
+  PLA_CUDA(cudaMemcpyToSymbol(g_device_faults, &zero, sizeof(unsigned int)));
+  return PLA_OK;
+}
+
+}  // extern "C"

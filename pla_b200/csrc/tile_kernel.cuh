@@ -1,0 +1,161 @@
+// Plane-tile kernel: 7x7 correlation over a stack of dense planes
+// (the single-step stencil of data/stencil_7x7.py, NCHW depthwise planes of
+// data/depthwise_conv_7x7.py with wide rows, and one Jacobi step of the
+// iterated stencil, whole grid or one row band).
+//
+// Design (sm_100a):
+//  * persistent CTAs (grid = #SMs x resident CTAs) walk a flat list of
+//    TH x TW output tiles, plane-major then row-major;
+//  * each tile's (TH+6) x (TW+8) input window is one 3-D TMA tile load
+//    (cp.async.bulk.tensor, no multicast) into a 2-stage shared-memory ring
+//    guarded by mbarriers, so the next tile streams in while this one is
+//    computed; TMA's out-of-bounds zero fill supplies the zero padding;
+//  * 4 warps x 32 lanes; a thread owns R rows x 4 columns of outputs, loads
+//    each input row of its window once with three 128-bit (fp32) or 64-bit
+//    (16-bit types) shared loads and applies it to every output row it
+//    touches (the 7-wide window is reused across the 4 columns in registers);
+//  * the 49 taps of the current plane's filter live in registers; fp32 FMA
+//    in row-major tap order; bias added in fp32; 128/64-bit vector stores.
+#pragma once
+
+#include "pla_common.cuh"
+
+namespace pla {
+
+constexpr int kTileThreads = 128;
+constexpr int kTileW = 128;  // output columns per tile (32 lanes x 4)
+
+template <typename T, int R>
+struct TileGeom {
+  static constexpr int TH = 4 * R;           // output rows per tile
+  static constexpr int ROWS = TH + 6;        // input rows per tile (3-row halo)
+  static constexpr int PITCH = kTileW + 8;   // input columns (4 left + 4 right)
+  static constexpr uint32_t BYTES = ROWS * PITCH * sizeof(T);
+  static constexpr uint32_t STAGE = (BYTES + 127u) & ~127u;
+  static constexpr uint32_t SMEM = 2 * STAGE + 2 * sizeof(uint64_t);
+};
+
+struct TileArgs {
+  const void* w;            // [C][49] taps
+  const void* b;            // [C] or nullptr
+  void* y;                  // output base (row 0 of output plane 0)
+  int planes;               // planes in the stack (tensor-map z extent)
+  int C;                    // filter index of plane p is p % C
+  int W;                    // plane width (output columns)
+  int row_begin, row_end;   // output rows computed: [row_begin, row_end)
+  int in_row_shift;         // input row (tensor-map y) of output row r is r + in_row_shift
+  int tiles_x, tiles_y;     // tiles per plane
+  long long total_tiles;    // planes * tiles_y * tiles_x
+  long long y_plane_stride; // elements
+  long long y_row_stride;   // elements
+};
+
+template <typename T, int R>
+__global__ void __launch_bounds__(kTileThreads, 4)
+    tile_kernel(const __grid_constant__ CUtensorMap tmap, const TileArgs a) {
+  using G = TileGeom<T, R>;
+  extern __shared__ __align__(128) unsigned char smem[];
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 2 * G::STAGE);
+
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int warp = tid >> 5;
+
+  if (tid == 0) {
+    prefetch_tensormap(&tmap);
+    mbar_init(&bars[0], 1);
+    mbar_init(&bars[1], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  const long long total = a.total_tiles;
+  const long long stride = gridDim.x;
+  long long t = blockIdx.x;
+
+  auto issue = [&](long long tile, int stage) {
+    const int tx = static_cast<int>(tile % a.tiles_x);
+    const long long q = tile / a.tiles_x;
+    const int ty = static_cast<int>(q % a.tiles_y);
+    const int plane = static_cast<int>(q / a.tiles_y);
+    const int x0 = tx * kTileW - 4;
+    const int y0 = a.row_begin + ty * G::TH + a.in_row_shift - kHalo;
+    fence_proxy_async_smem();
+    mbar_arrive_expect_tx(&bars[stage], G::BYTES);
+    tma_load_3d(smem + stage * G::STAGE, &tmap, &bars[stage], x0, y0, plane);
+  };
+
+  if (tid == 0 && t < total) issue(t, 0);
+
+  const T* wt_base = static_cast<const T*>(a.w);
+  const T* b_base = static_cast<const T*>(a.b);
+  float wt[kTaps];
+  int cur_c = -1;
+  float bias = 0.f;
+
+  for (int it = 0; t < total; ++it, t += stride) {
+    const int stage = it & 1;
+    if (tid == 0 && t + stride < total) issue(t + stride, stage ^ 1);
+
+    const int tx = static_cast<int>(t % a.tiles_x);
+    const long long q = t / a.tiles_x;
+    const int ty = static_cast<int>(q % a.tiles_y);
+    const int plane = static_cast<int>(q / a.tiles_y);
+    const int c = plane % a.C;
+    if (c != cur_c) {
+      cur_c = c;
+#pragma unroll
+      for (int k = 0; k < kTaps; ++k) wt[k] = to_acc(wt_base[c * kTaps + k]);
+      bias = b_base ? to_acc(b_base[c]) : 0.f;
+    }
+
+    mbar_wait_bounded(&bars[stage], (it >> 1) & 1);
+
+    const T* s = reinterpret_cast<const T*>(smem + stage * G::STAGE) + (warp * R) * G::PITCH + 4 * lane;
+    float acc[R][4];
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[r][j] = 0.f;
+
+#pragma unroll
+    for (int ir = 0; ir < R + 6; ++ir) {
+      float v[12];
+      load_row12(s + ir * G::PITCH, v);
+#pragma unroll
+      for (int kx = 0; kx < 7; ++kx) {
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          const int ky = ir - r;
+          if (ky >= 0 && ky < 7) {
+            const float wv = wt[ky * 7 + kx];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) acc[r][j] = fma_rn(v[j + kx + 1], wv, acc[r][j]);
+          }
+        }
+      }
+    }
+    // Every thread is done with this stage before it is refilled.
+    __syncthreads();
+
+    const int ox = tx * kTileW + 4 * lane;
+    if (ox < a.W) {
+      T* yp = static_cast<T*>(a.y) + plane * a.y_plane_stride + ox;
+      const int oy0 = a.row_begin + ty * G::TH + warp * R;
+      const bool has_bias = b_base != nullptr;
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        const int oy = oy0 + r;
+        if (oy < a.row_end) {
+          float o0 = acc[r][0], o1 = acc[r][1], o2 = acc[r][2], o3 = acc[r][3];
+          if (has_bias) {
+            o0 += bias; o1 += bias; o2 += bias; o3 += bias;
+          }
+          store4(yp + oy * a.y_row_stride, o0, o1, o2, o3);
+        }
+      }
+    }
+  }
+}
+
+}  // namespace pla

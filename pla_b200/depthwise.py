@@ -1,0 +1,94 @@
+"""Depthwise 7x7 convolution with the reference's KernelBench module contract.
+
+Drop-in for the generated depthwise modules of the reference
+(``data/depthwise_conv_7x7_cuda/model_cutlass_autotune_v6.py:495-524``,
+``model_cutlass.py:316-345``); the op they replace is
+``data/depthwise_conv_7x7.py:15-29``
+(``nn.Conv2d(C, C, k, stride, padding, groups=C, bias)``).  Same names:
+``ModelNew(in_channels, kernel_size, stride=1, padding=1, bias=False)`` with a
+``conv2d`` submodule (``conv2d.weight`` [C,1,7,7], ``conv2d.bias`` [C] when
+bias=True), ``get_inputs()``, ``get_init_inputs()``.
+
+Beyond the reference kernels (fp16/fp32, NCHW, no bias, weights repacked to
+[C,8,80]): fp32 / bf16 / fp16 / fp64, NCHW and channels_last (NHWC), optional
+bias, and no weight repack (the kernels read the module's own weight).
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+
+
+def depthwise7x7(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None,
+                 out: torch.Tensor | None = None) -> torch.Tensor:
+    """y = conv2d(x, weight, bias, stride=1, padding=3, groups=C) for CUDA x [N,C,H,W].
+
+    A channels_last input runs the NHWC kernels and returns channels_last (as
+    torch does); a contiguous input runs NCHW; anything else is made
+    contiguous first.
+    """
+    if not isinstance(x, torch.Tensor) or not x.is_cuda:
+        raise ValueError("depthwise7x7 requires a CUDA input")
+    if x.dim() != 4:
+        raise RuntimeError("input must have shape [N,C,H,W]")
+    N, C, H, W = x.shape
+    if not weight.is_cuda or weight.device != x.device:
+        raise RuntimeError("weight must be a CUDA tensor on the input's device")
+    if weight.numel() != C * 49 or (weight.dim() == 4 and tuple(weight.shape) != (C, 1, 7, 7)):
+        raise RuntimeError("weight must have shape [C,1,7,7]")
+    if weight.dtype != x.dtype:
+        raise RuntimeError("dtype mismatch")
+    if x.dtype not in _lib.DTYPE_CODE:
+        raise RuntimeError("unsupported dtype")
+    if bias is not None and (not bias.is_cuda or bias.device != x.device or bias.dtype != x.dtype
+                             or bias.numel() != C):
+        raise RuntimeError("bias device/dtype/shape mismatch")
+    if x.is_contiguous():
+        layout, fmt = _lib.PLA_NCHW, torch.contiguous_format
+    elif x.is_contiguous(memory_format=torch.channels_last):
+        layout, fmt = _lib.PLA_NHWC, torch.channels_last
+    else:
+        x = x.contiguous()
+        layout, fmt = _lib.PLA_NCHW, torch.contiguous_format
+    if out is None:
+        out = torch.empty(x.shape, dtype=x.dtype, device=x.device, memory_format=fmt)
+    elif out.shape != x.shape or not out.is_contiguous(memory_format=fmt) or out.dtype != x.dtype:
+        raise RuntimeError("out must match x's shape, dtype and memory format")
+    if out.numel() == 0:
+        return out
+    weight = weight.detach().contiguous()
+    bias = None if bias is None else bias.detach().contiguous()
+    with torch.cuda.device(x.device):
+        st = _lib.lib().pla_depthwise7x7_forward(
+            x.data_ptr(), weight.data_ptr(), _lib.ptr(bias), out.data_ptr(), N, C, H, W,
+            _lib.DTYPE_CODE[x.dtype], layout, _lib.stream_ptr(x.device))
+    _lib.check(st, "pla_depthwise7x7_forward")
+    return out
+
+
+class ModelNew(torch.nn.Module):
+    """KernelBench drop-in for data/depthwise_conv_7x7.py's Model (parameter ``conv2d``)."""
+
+    def __init__(self, in_channels: int, kernel_size: int, stride: int = 1, padding: int = 1,
+                 bias: bool = False):
+        super().__init__()
+        if kernel_size != 7 or stride != 1 or padding != 3:
+            raise ValueError("only kernel_size=7, stride=1, padding=3 is supported")
+        self.conv2d = torch.nn.Conv2d(in_channels, in_channels, 7, stride=1, padding=3,
+                                      groups=in_channels, bias=bias)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        return depthwise7x7(x, self.conv2d.weight, self.conv2d.bias)
+
+
+# Harness shape of the reference problem (data/depthwise_conv_7x7.py:64-85).
+batch_size, in_channels, kernel_size, height, width, stride, padding = 1, 8, 7, 2048, 2048, 1, 3
+
+
+def get_inputs():
+    return [torch.rand(batch_size, in_channels, height, width)]
+
+
+def get_init_inputs():
+    return [in_channels, kernel_size, stride, padding]

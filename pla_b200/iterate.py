@@ -1,0 +1,191 @@
+"""Iterated 7x7 stencil: u_{t+1} = stencil(u_t), zero Dirichlet boundary.
+
+No reference function exists for the iteration: the reference op is
+data/stencil_7x7.py:10-12 applied once.  Iterating it with its zero padding
+re-applied every step is the Jacobi scheme with a zero boundary.
+
+* ``stencil7x7_iterate`` — one device, ping-pong between the output and one
+  scratch plane (``pla_stencil7x7_iterate``).
+* ``BandedStencil`` — the grid split into row bands, one band per rank of a
+  process group (one process per GPU).  Each band lives in two
+  (rows + 6) x W buffers whose 3 top / 3 bottom rows are halos.  A step
+  computes the 3 edge rows at each end of the band first, hands them to the
+  neighbours (NCCL send/recv on a side stream into their halo rows) and
+  computes the interior rows while the exchange is in flight.  Bands at the
+  top / bottom of the grid keep zero halos (the Dirichlet boundary).  Every
+  point is computed exactly as on one device, so the result is bit-identical
+  to ``stencil7x7_iterate`` for any number of ranks.
+"""
+from __future__ import annotations
+
+from typing import Callable, Optional
+
+import torch
+import torch.distributed as dist
+
+from . import _lib
+
+
+def stencil7x7_iterate(x: torch.Tensor, weight: torch.Tensor, steps: int, bias: torch.Tensor | None = None,
+                       out: torch.Tensor | None = None, scratch: torch.Tensor | None = None) -> torch.Tensor:
+    """Apply the 7x7 stencil `steps` times to the CUDA grid x [H, W] (fp32/bf16/fp16)."""
+    if not isinstance(x, torch.Tensor) or not x.is_cuda:
+        raise ValueError("stencil7x7_iterate requires a CUDA input")
+    if x.dim() != 2 or not x.is_contiguous():
+        raise RuntimeError("expected a contiguous [H, W] grid")
+    if steps < 0:
+        raise ValueError("steps must be >= 0")
+    if weight.numel() != 49 or weight.dtype != x.dtype or weight.device != x.device:
+        raise RuntimeError("weight must be one 7x7 filter of x's dtype and device")
+    if bias is not None and (bias.numel() != 1 or bias.dtype != x.dtype or bias.device != x.device):
+        raise RuntimeError("bias device/dtype/shape mismatch")
+    H, W = x.shape
+    if out is None:
+        out = torch.empty_like(x)
+    if scratch is None:
+        scratch = torch.empty_like(x)
+    weight = weight.detach().contiguous()
+    bias = None if bias is None else bias.detach().contiguous()
+    with torch.cuda.device(x.device):
+        st = _lib.lib().pla_stencil7x7_iterate(
+            x.data_ptr(), weight.data_ptr(), _lib.ptr(bias), out.data_ptr(), scratch.data_ptr(), H, W, steps,
+            _lib.DTYPE_CODE[x.dtype], _lib.stream_ptr(x.device))
+    _lib.check(st, "pla_stencil7x7_iterate")
+    return out
+
+
+def band_rows(total_rows: int, world: int, rank: int) -> tuple[int, int]:
+    """Rows [r0, r1) of band `rank` when `total_rows` are split into `world` bands.
+
+    The first total_rows % world bands get one extra row, so band sizes differ
+    by at most one.
+    """
+    if world <= 0 or not 0 <= rank < world:
+        raise ValueError("bad rank/world")
+    base, extra = divmod(total_rows, world)
+    r0 = rank * base + min(rank, extra)
+    return r0, r0 + base + (1 if rank < extra else 0)
+
+
+StepFn = Callable[[torch.Tensor, torch.Tensor, int, int], None]
+
+
+def _cuda_band_step(weight: torch.Tensor, bias: Optional[torch.Tensor]) -> StepFn:
+    L = _lib.lib()
+    code = _lib.DTYPE_CODE[weight.dtype]
+
+    def step(src: torch.Tensor, dst: torch.Tensor, row_begin: int, row_end: int) -> None:
+        rows, W = src.shape[0] - 6, src.shape[1]
+        st = L.pla_stencil7x7_band_step(src.data_ptr(), weight.data_ptr(), _lib.ptr(bias), dst.data_ptr(), rows,
+                                        W, row_begin, row_end, code, _lib.stream_ptr(src.device))
+        _lib.check(st, "pla_stencil7x7_band_step")
+
+    return step
+
+
+class BandedStencil:
+    """Row-band partitioned iterated stencil over a process group.
+
+    ``step_fn(src, dst, row_begin, row_end)`` computes band rows
+    [row_begin, row_end) of one step from band buffer `src` into `dst`; the
+    default is the CUDA kernel.  The halo exchange uses the group's P2P
+    send/recv (NCCL on GPUs; gloo ranks on the CPU for the tests).
+    """
+
+    def __init__(self, H: int, W: int, weight: torch.Tensor, bias: torch.Tensor | None = None,
+                 group=None, device: torch.device | None = None, step_fn: StepFn | None = None,
+                 overlap: bool = True):
+        self.group = group
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.H, self.W = H, W
+        self.r0, self.r1 = band_rows(H, self.world, self.rank)
+        self.rows = self.r1 - self.r0
+        if self.world > 1 and H < 3 * self.world:
+            raise ValueError("every band needs at least 3 rows (H >= 3 * world size)")
+        self.device = device if device is not None else weight.device
+        self.dtype = weight.dtype
+        self.weight = weight.detach().reshape(49).contiguous()
+        self.bias = None if bias is None else bias.detach().reshape(1).contiguous()
+        self.step_fn = step_fn or _cuda_band_step(self.weight, self.bias)
+        self.bufs = [torch.zeros(self.rows + 6, W, dtype=self.dtype, device=self.device) for _ in range(2)]
+        self.cur = 0
+        self.overlap = overlap and self.device.type == "cuda" and self.rows >= 12
+        self.comm_stream = torch.cuda.Stream(self.device) if self.device.type == "cuda" else None
+        self.up = self.rank - 1 if self.rank > 0 else None
+        self.down = self.rank + 1 if self.rank < self.world - 1 else None
+
+    def _global(self, peer: int) -> int:
+        return peer if self.group is None else dist.get_global_rank(self.group, peer)
+
+    # -- state -------------------------------------------------------------
+    def load(self, grid: torch.Tensor) -> None:
+        """Copy this rank's band (and its halo rows) out of the full grid [H, W]."""
+        b = self.bufs[self.cur]
+        b.zero_()
+        a0, a1 = max(0, self.r0 - 3), min(self.H, self.r1 + 3)
+        b[3 - (self.r0 - a0):3 + self.rows + (a1 - self.r1)].copy_(grid[a0:a1])
+        self.bufs[1 - self.cur].zero_()
+
+    def band(self) -> torch.Tensor:
+        """This rank's current band rows [rows, W] (a view)."""
+        return self.bufs[self.cur][3:3 + self.rows]
+
+    def gather(self) -> Optional[torch.Tensor]:
+        """Full grid on rank 0 (None elsewhere)."""
+        band = self.band().contiguous()
+        if self.world == 1:
+            return band.clone()
+        sizes = [band_rows(self.H, self.world, r) for r in range(self.world)]
+        if self.rank == 0:
+            out = torch.empty(self.H, self.W, dtype=self.dtype, device=self.device)
+            out[self.r0:self.r1].copy_(band)
+            for r in range(1, self.world):
+                a, b = sizes[r]
+                if b > a:
+                    t = torch.empty(b - a, self.W, dtype=self.dtype, device=self.device)
+                    dist.recv(t, self._global(r), group=self.group)
+                    out[a:b].copy_(t)
+            return out
+        if self.rows > 0:
+            dist.send(band, self._global(0), group=self.group)
+        return None
+
+    # -- one Jacobi step -----------------------------------------------------
+    def _exchange_ops(self, dst: torch.Tensor):
+        ops = []
+        R = self.rows
+        if self.up is not None:
+            ops.append(dist.P2POp(dist.isend, dst[3:6], self._global(self.up), self.group))
+            ops.append(dist.P2POp(dist.irecv, dst[0:3], self._global(self.up), self.group))
+        if self.down is not None:
+            ops.append(dist.P2POp(dist.isend, dst[R:R + 3], self._global(self.down), self.group))
+            ops.append(dist.P2POp(dist.irecv, dst[R + 3:R + 6], self._global(self.down), self.group))
+        return ops
+
+    def step(self) -> None:
+        src, dst = self.bufs[self.cur], self.bufs[1 - self.cur]
+        R = self.rows
+        if self.overlap and self.world > 1:
+            compute = torch.cuda.current_stream(self.device)
+            # 1) the rows the neighbours need, 2) hand them over on the side
+            #    stream while 3) the interior is computed, 4) join.
+            self.step_fn(src, dst, 0, 3)
+            self.step_fn(src, dst, R - 3, R)
+            self.comm_stream.wait_stream(compute)
+            with torch.cuda.stream(self.comm_stream):
+                for w in dist.batch_isend_irecv(self._exchange_ops(dst)):
+                    w.wait()
+            self.step_fn(src, dst, 3, R - 3)
+            compute.wait_stream(self.comm_stream)
+        else:
+            self.step_fn(src, dst, 0, R)
+            ops = self._exchange_ops(dst)
+            if ops:
+                for w in dist.batch_isend_irecv(ops):
+                    w.wait()
+        self.cur = 1 - self.cur
+
+    def run(self, steps: int) -> None:
+        for _ in range(steps):
+            self.step()

@@ -1,0 +1,81 @@
+"""The C-ABI library loads without a GPU and exports every declared symbol."""
+import ctypes
+import os
+import re
+
+import pytest
+import torch
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "pla_b200.h")
+
+
+def declared_symbols():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"PLA_API\s+[\w\s\*]+?\b(pla_\w+)\s*\(", text)))
+
+
+def test_header_declares_entry_points():
+    names = declared_symbols()
+    for must in ("pla_stencil7x7_forward", "pla_depthwise7x7_forward", "pla_stencil7x7_iterate",
+                 "pla_stencil7x7_band_step", "pla_status_string"):
+        assert must in names
+
+
+def test_library_exports_every_declared_symbol():
+    from pla_b200 import _lib
+
+    L = _lib.lib()
+    for name in declared_symbols():
+        assert hasattr(L, name), name
+    assert set(declared_symbols()) == set(_lib.SIGNATURES)
+
+
+def test_status_strings_and_version():
+    from pla_b200 import _lib
+
+    L = _lib.lib()
+    assert L.pla_status_string(0) == b"ok"
+    assert b"unsupported" in L.pla_status_string(2)
+    assert L.pla_status_string(12345) == b"unknown status"
+    assert L.pla_version() >> 16 == 1
+
+
+def test_argument_validation_needs_no_device():
+    # Invalid enums / negative sizes are rejected before any CUDA call.
+    from pla_b200 import _lib
+
+    L = _lib.lib()
+    assert L.pla_stencil7x7_forward(None, None, None, None, 1, 1, 1, 1, 1, 1, 99, None) == 2
+    assert L.pla_depthwise7x7_forward(None, None, None, None, -1, 1, 1, 1, 1, 0, None) == 1
+    assert L.pla_depthwise7x7_forward(None, None, None, None, 1, 1, 1, 1, 1, 7, None) == 1
+    assert L.pla_stencil7x7_band_step(None, None, None, None, 4, 8, 3, 2, 1, None) == 1
+    # empty problems are a no-op success
+    assert L.pla_stencil7x7_forward(None, None, None, None, 0, 5, 5, 25, 5, 1, 1, None) == 0
+
+
+def test_ops_refuse_cpu_tensors():
+    from pla_b200 import depthwise, stencil
+
+    with pytest.raises(ValueError):
+        stencil.ModelNew()(torch.rand(1, 1, 8, 8))
+    with pytest.raises(ValueError):
+        depthwise.ModelNew(4, 7, 1, 3)(torch.rand(1, 4, 8, 8))
+
+
+def test_module_interfaces_match_reference():
+    from pla_b200 import depthwise, stencil
+
+    # data/stencil_direct_cuda_v7/test_stencil.py:23
+    assert set(stencil.ModelNew().state_dict()) == {"conv1.weight", "conv1.bias"}
+    assert stencil.get_init_inputs() == []
+    # data/depthwise_conv_7x7.py:15-17, get_init_inputs() -> [C, 7, 1, 3]
+    m = depthwise.ModelNew(*depthwise.get_init_inputs())
+    assert set(m.state_dict()) == {"conv2d.weight"}
+    assert tuple(m.conv2d.weight.shape) == (8, 1, 7, 7)
+    mb = depthwise.ModelNew(16, 7, 1, 3, bias=True)
+    assert set(mb.state_dict()) == {"conv2d.weight", "conv2d.bias"}
+    with pytest.raises(ValueError):
+        depthwise.ModelNew(8, 3, 1, 1)
+    with pytest.raises(ValueError):
+        depthwise.ModelNew(8, 7, 1, 1)  # the reference default padding=1 is not a 7x7 "same" conv

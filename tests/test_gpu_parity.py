@@ -1,0 +1,276 @@
+"""GPU parity: the sm_100a kernels (through the C ABI) against the CPU oracle
+and against the reference modules' golden vectors.
+
+The CUDA kernels and the oracle evaluate each output point in the same fixed
+order (row-major taps, fp32 fma, then + bias, one rounding), so they must agree
+bit for bit (``torch.equal``); the golden vectors (reference torch.nn.Conv2d on
+the CPU, a different summation order) are matched within the north star's
+tolerances: rtol = atol = 1e-5 for fp32, 2e-2 for bf16 (and the reference
+tests' 2e-3 for fp16, 1e-10 for fp64,
+data/stencil_direct_cuda_v7/test_stencil.py:39-40).
+"""
+import pytest
+import torch
+import torch.nn.functional as F
+
+from oracle import oracle
+from tests.golden_util import TOL, load_cases
+
+pytestmark = pytest.mark.gpu
+
+CASES = load_cases()
+DEV = "cuda:0"
+
+
+def _gpu_copy(t: torch.Tensor) -> torch.Tensor:
+    """Copy a CPU tensor to the GPU keeping its strides (sliced/transposed layouts survive)."""
+    g = torch.empty_strided(t.shape, t.stride(), dtype=t.dtype, device=DEV)
+    g.copy_(t)
+    return g
+
+
+def _assert_equal(gpu: torch.Tensor, ref: torch.Tensor):
+    got = gpu.cpu()
+    assert got.shape == ref.shape
+    if not torch.equal(got, ref):
+        diff = (got.double() - ref.double()).abs()
+        raise AssertionError(f"not bit-identical: {int((diff > 0).sum())} of {diff.numel()} differ, "
+                             f"max |diff| {diff.max().item():.3e}")
+
+
+# --------------------------------------------------------------------------
+# golden vectors (reference modules) -> GPU, and GPU == oracle bit for bit
+# --------------------------------------------------------------------------
+@pytest.mark.parametrize("case", CASES, ids=[c.name for c in CASES])
+def test_golden_cases(case):
+    from pla_b200 import depthwise7x7, stencil7x7, stencil7x7_iterate
+
+    x = _gpu_copy(case.x)
+    w = case.w.to(DEV)
+    b = None if case.b is None else case.b.to(DEV)
+    if case.op == "stencil":
+        y = stencil7x7(x, w.reshape(1, 1, 7, 7), b)
+        ref = oracle.stencil7x7(case.x, case.w, case.b)
+    elif case.op == "depthwise":
+        C = case.shape[1]
+        y = depthwise7x7(x, w.reshape(C, 1, 7, 7), b)
+        ref = oracle.depthwise7x7(case.x, case.w.reshape(C, 1, 7, 7), case.b)
+        if case.layout == "nhwc":
+            assert y.is_contiguous(memory_format=torch.channels_last)
+    else:
+        y = stencil7x7_iterate(x.contiguous(), w, case.steps, b)
+        ref = oracle.stencil7x7_iterate(case.x, case.w, case.steps, case.b)
+    torch.cuda.synchronize()
+    _assert_equal(y, ref)
+    if case.op == "iterate":
+        scale = case.y.abs().max().item()
+        torch.testing.assert_close(y.cpu() / scale, case.y / scale, rtol=1e-5, atol=1e-5)
+    else:
+        torch.testing.assert_close(y.cpu().float(), case.y.float(), rtol=case.tol, atol=case.tol)
+
+
+# --------------------------------------------------------------------------
+# the reference's own stencil test matrix
+# (data/stencil_direct_cuda_v7/test_stencil.py:27-58)
+# --------------------------------------------------------------------------
+def _v7_cases():
+    g = torch.Generator().manual_seed(42)
+    r = lambda *s: torch.randn(*s, generator=g)  # noqa: E731
+    return [r(2, 1, 1, 1), r(1, 7, 9), r(2, 1, 17, 257), r(1, 1, 48, 769), r(1, 1, 48, 1536),
+            r(1, 1, 35, 10240), r(2, 1, 17, 516), r(1, 1, 2, 4), r(2, 1, 35, 518)[:, :, ::2, ::2],
+            r(2, 1, 259, 19).transpose(-1, -2), r(4, 1, 9, 13)[::2], torch.empty(0, 1, 9, 13)]
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16, torch.float32, torch.float64])
+@pytest.mark.parametrize("use_bias", [True, False])
+def test_reference_v7_matrix(dtype, use_bias):
+    from pla_b200.stencil import ModelNew
+
+    tol = {torch.float16: 2e-3, torch.bfloat16: 2e-2, torch.float32: 2e-5, torch.float64: 1e-10}[dtype]
+    torch.manual_seed(0)
+    model = ModelNew().to(DEV).to(dtype)
+    if not use_bias:
+        model.conv1.bias = None
+    acc = torch.float64 if dtype == torch.float64 else torch.float32
+    for cpu_x in _v7_cases():
+        cpu_x = cpu_x.to(dtype)
+        x = _gpu_copy(cpu_x)
+        with torch.no_grad():
+            y = model(x)
+            bias = model.conv1.bias
+            expected = F.conv2d(cpu_x.to(acc), model.conv1.weight.cpu().to(acc),
+                                None if bias is None else bias.cpu().to(acc), padding=3).to(dtype)
+        assert y.shape == x.shape and y.is_contiguous()
+        torch.testing.assert_close(y.cpu(), expected, atol=tol, rtol=tol)
+        if dtype != torch.float64 and cpu_x.numel():
+            ref = oracle.stencil7x7(cpu_x, model.conv1.weight.detach().cpu(),
+                                    None if bias is None else bias.detach().cpu())
+            _assert_equal(y, ref)
+
+
+def test_updated_weights_side_stream_and_empty():
+    # data/stencil_cuda_v2/test_stencil.py:85-96
+    from pla_b200.stencil import ModelNew
+
+    for dtype in (torch.float16, torch.float32):
+        model = ModelNew().to(DEV).to(dtype)
+        with torch.no_grad():
+            model.conv1.weight.zero_()
+            model.conv1.bias.fill_(0.25)
+            x = torch.randn(1, 1, 7, 11, device=DEV, dtype=dtype)
+            stream = torch.cuda.Stream()
+            stream.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(stream):
+                y = model(x)
+            torch.cuda.current_stream().wait_stream(stream)
+            torch.testing.assert_close(y, torch.full_like(y, 0.25), atol=0, rtol=0)
+            for shape in [(0, 1, 3, 4), (1, 1, 0, 4), (1, 1, 3, 0)]:
+                assert model(torch.empty(shape, device=DEV, dtype=dtype)).shape == shape
+
+
+# --------------------------------------------------------------------------
+# BASELINE configurations at full size, bit-exact against the oracle
+# --------------------------------------------------------------------------
+def _dw_inputs(seed, shape, dtype, bias=True):
+    g = torch.Generator().manual_seed(seed)
+    N, C, H, W = shape
+    x = torch.randn(shape, generator=g).to(dtype)
+    w = (torch.randn(C, 1, 7, 7, generator=g) / 7).to(dtype)
+    b = (torch.randn(C, generator=g) * 0.1).to(dtype) if bias else None
+    return x, w, b
+
+
+@pytest.mark.parametrize("name,shape,dtype,layout,bias,seed", [
+    ("cfg1", (1, 96, 56, 56), torch.float32, "nchw", True, 0),
+    ("cfg3_nchw", (128, 384, 14, 14), torch.bfloat16, "nchw", True, 2),
+    ("cfg3_nhwc", (128, 384, 14, 14), torch.bfloat16, "nhwc", True, 2),
+    ("cfg4_s1", (256, 96, 56, 56), torch.bfloat16, "nchw", False, 3),
+    ("cfg4_s2", (256, 192, 28, 28), torch.bfloat16, "nchw", False, 3),
+    ("cfg4_s3", (256, 384, 14, 14), torch.bfloat16, "nchw", False, 3),
+    ("cfg4_s4", (256, 768, 7, 7), torch.bfloat16, "nchw", False, 3),
+    ("cfg4_s1_nhwc", (64, 96, 56, 56), torch.bfloat16, "nhwc", False, 3),
+    ("dw_2048_f32", (1, 8, 2048, 2048), torch.float32, "nchw", False, 5),
+])
+def test_depthwise_configs_full_size(name, shape, dtype, layout, bias, seed):
+    from pla_b200.depthwise import ModelNew
+
+    x, w, b = _dw_inputs(seed, shape, dtype, bias)
+    if layout == "nhwc":
+        x = x.contiguous(memory_format=torch.channels_last)
+    m = ModelNew(shape[1], 7, 1, 3, bias=bias).to(DEV).to(dtype)
+    with torch.no_grad():
+        m.conv2d.weight.copy_(w)
+        if bias:
+            m.conv2d.bias.copy_(b)
+        y = m(x.to(DEV))
+    ref = oracle.depthwise7x7(x, w, b)
+    _assert_equal(y, ref)
+    tol = TOL["bf16" if dtype == torch.bfloat16 else "f32"]
+    # and the reference module's arithmetic (fp32 conv, one cast) within tolerance
+    if shape[0] * shape[1] <= 128 * 384:
+        acc = F.conv2d(x.float(), w.float(), None if b is None else b.float(), padding=3, groups=shape[1])
+        torch.testing.assert_close(y.cpu().float(), acc.to(dtype).float(), rtol=tol, atol=tol)
+
+
+def test_stencil_cfg2_full_size():
+    from pla_b200.stencil import ModelNew
+
+    g = torch.Generator().manual_seed(1)
+    x = torch.rand(1, 1, 4096, 4096, generator=g) * 2 - 1
+    w = (torch.rand(1, 1, 7, 7, generator=g) * 2 - 1) / 49
+    b = (torch.rand(1, generator=g) * 2 - 1) / 49
+    m = ModelNew().to(DEV)
+    with torch.no_grad():
+        m.conv1.weight.copy_(w)
+        m.conv1.bias.copy_(b)
+        y = m(x.to(DEV))
+    _assert_equal(y, oracle.stencil7x7(x, w, b))
+    ref = F.conv2d(x, w, b, padding=3)
+    torch.testing.assert_close(y.cpu(), ref, rtol=1e-5, atol=1e-5)
+
+
+# --------------------------------------------------------------------------
+# iterated stencil
+# --------------------------------------------------------------------------
+def _cfg5_inputs(H, W, seed=4):
+    g = torch.Generator().manual_seed(seed)
+    x = torch.rand(H, W, generator=g) * 2 - 1
+    w = torch.rand(7, 7, generator=g) * 2 - 1
+    return x, w / w.sum()
+
+
+@pytest.mark.parametrize("H,W,steps", [(512, 512, 100), (300, 260, 7), (64, 64, 0), (33, 128, 1)])
+def test_iterate_matches_oracle_bitwise(H, W, steps):
+    from pla_b200 import stencil7x7_iterate
+
+    x, w = _cfg5_inputs(H, W)
+    y = stencil7x7_iterate(x.to(DEV), w.to(DEV), steps)
+    _assert_equal(y, oracle.stencil7x7_iterate(x, w, steps))
+
+
+def test_iterate_in_place_and_odd_steps():
+    from pla_b200 import stencil7x7_iterate
+
+    x, w = _cfg5_inputs(128, 96)
+    ref = oracle.stencil7x7_iterate(x, w, 5)
+    xd = x.to(DEV)
+    y = stencil7x7_iterate(xd, w.to(DEV), 5, out=xd)
+    assert y.data_ptr() == xd.data_ptr()
+    _assert_equal(y, ref)
+
+
+def test_band_step_equals_full_step():
+    from pla_b200 import _lib
+
+    x, w = _cfg5_inputs(200, 256)
+    full = oracle.stencil7x7(x.view(1, 1, 200, 256), w).view(200, 256)
+    r0, r1 = 57, 131
+    rows = r1 - r0
+    band_in = torch.zeros(rows + 6, 256)
+    band_in[:] = x[r0 - 3:r1 + 3]
+    src = band_in.to(DEV)
+    dst = torch.full((rows + 6, 256), 7.0, device=DEV)
+    wd = w.to(DEV).contiguous()
+    L = _lib.lib()
+    for a, b in [(0, 3), (rows - 3, rows), (3, rows - 3)]:
+        st = L.pla_stencil7x7_band_step(src.data_ptr(), wd.data_ptr(), None, dst.data_ptr(), rows, 256, a, b,
+                                        1, torch.cuda.current_stream().cuda_stream)
+        assert st == 0
+    out = dst.cpu()
+    _assert_equal(out[3:3 + rows], full[r0:r1])
+    assert torch.all(out[:3] == 7.0) and torch.all(out[rows + 3:] == 7.0)  # halos untouched
+
+
+def test_cfg5_full_size_first_steps():
+    """32768^2 grid: two GPU steps against the oracle on three row bands."""
+    from pla_b200 import stencil7x7_iterate
+
+    H = W = 32768
+    x, w = _cfg5_inputs(H, W)
+    xd = x.to(DEV)
+    y1 = stencil7x7_iterate(xd, w.to(DEV), 1)
+    y2 = stencil7x7_iterate(xd, w.to(DEV), 2)
+    for r0, r1 in [(0, 16), (16380, 16420), (H - 16, H)]:
+        ref1 = oracle.stencil7x7_rows(x, w, r0, r1)
+        _assert_equal(y1[r0:r1], ref1)
+        # step 2 on the band needs step-1 rows r0-3 .. r1+2, taken from the GPU
+        a0, a1 = max(0, r0 - 3), min(H, r1 + 3)
+        u1 = y1[a0:a1].cpu()
+        ref2 = oracle.stencil7x7_rows(u1, w, r0 - a0, r1 - a0) if (a0 == 0 or a1 == H) else None
+        if ref2 is None:
+            sub = oracle.stencil7x7(u1.view(1, 1, a1 - a0, W), w).view(a1 - a0, W)
+            ref2 = sub[3:3 + (r1 - r0)]
+        _assert_equal(y2[r0:r1], ref2)
+    del xd, y1, y2
+    torch.cuda.empty_cache()
+
+
+def test_no_device_faults_recorded():
+    import ctypes
+
+    from pla_b200 import _lib
+
+    torch.cuda.synchronize()
+    v = ctypes.c_uint(123)
+    assert _lib.lib().pla_read_device_faults(ctypes.byref(v)) == 0
+    assert v.value == 0
