@@ -6,7 +6,7 @@
 // Design (sm_100a):
 //  * persistent CTAs (grid = #SMs x resident CTAs) walk a flat list of
 //    TH x TW output tiles, plane-major then row-major;
-//  * each tile's (TH+6) x (TW+8) input window is one 3-D TMA tile load
+//  * each tile's (TH+6) x (TW+2*LEFT) input window is one 3-D TMA tile load
 //    (cp.async.bulk.tensor, no multicast) into a 2-stage shared-memory ring
 //    guarded by mbarriers, so the next tile streams in while this one is
 //    computed; TMA's out-of-bounds zero fill supplies the zero padding;
@@ -25,11 +25,17 @@ namespace pla {
 constexpr int kTileThreads = 128;
 constexpr int kTileW = 128;  // output columns per tile (32 lanes x 4)
 
+// The TMA box starts LEFT columns left of the tile: LEFT * sizeof(T) == 16 B
+// keeps the innermost TMA coordinate 16-byte aligned (a hard TMA rule), and
+// LEFT >= 3 covers the halo.  The box is LEFT + 128 + LEFT wide.
 template <typename T, int R>
 struct TileGeom {
   static constexpr int TH = 4 * R;           // output rows per tile
   static constexpr int ROWS = TH + 6;        // input rows per tile (3-row halo)
-  static constexpr int PITCH = kTileW + 8;   // input columns (4 left + 4 right)
+  static constexpr int LEFT = 16 / sizeof(T);
+  static constexpr int PITCH = kTileW + 2 * LEFT;
+  static_assert(LEFT >= 4 && (LEFT * sizeof(T)) % 16 == 0, "TMA x must stay 16-byte aligned");
+  static_assert((PITCH * sizeof(T)) % 16 == 0, "TMA box inner extent must be a multiple of 16 B");
   static constexpr uint32_t BYTES = ROWS * PITCH * sizeof(T);
   static constexpr uint32_t STAGE = (BYTES + 127u) & ~127u;
   static constexpr uint32_t SMEM = 2 * STAGE + 2 * sizeof(uint64_t);
@@ -78,7 +84,7 @@ __global__ void __launch_bounds__(kTileThreads, 4)
     const long long q = tile / a.tiles_x;
     const int ty = static_cast<int>(q % a.tiles_y);
     const int plane = static_cast<int>(q / a.tiles_y);
-    const int x0 = tx * kTileW - 4;
+    const int x0 = tx * kTileW - G::LEFT;
     const int y0 = a.row_begin + ty * G::TH + a.in_row_shift - kHalo;
     fence_proxy_async_smem();
     mbar_arrive_expect_tx(&bars[stage], G::BYTES);
@@ -111,7 +117,9 @@ __global__ void __launch_bounds__(kTileThreads, 4)
 
     mbar_wait_bounded(&bars[stage], (it >> 1) & 1);
 
-    const T* s = reinterpret_cast<const T*>(smem + stage * G::STAGE) + (warp * R) * G::PITCH + 4 * lane;
+    // v[k] below is input column ox - 4 + k (ox = this thread's first output column).
+    const T* s = reinterpret_cast<const T*>(smem + stage * G::STAGE) + (warp * R) * G::PITCH + 4 * lane +
+                 (G::LEFT - 4);
     float acc[R][4];
 #pragma unroll
     for (int r = 0; r < R; ++r)
