@@ -93,6 +93,22 @@ PLA_API int pla_stencil7x7_forward(const void* x, const void* w, const void* b, 
                            int dtype, pla_stream_t stream);
 
 /*
+ * pla_stencil7x7_forward with the filter given by value: `taps` points to 49
+ * fp32 taps in HOST memory (row-major), `bias` to one host fp32 value or is
+ * NULL.  The taps travel in the kernel's parameter block, so the kernel reads
+ * them as uniform constant operands instead of holding them in registers
+ * (the fast path; same results bit for bit).  16-bit filters widen to fp32
+ * exactly.  Only inputs that qualify for the TMA path are accepted (unit
+ * column stride, 16-byte aligned rows); others return PLA_ERR_UNSUPPORTED
+ * and should use pla_stencil7x7_forward.  Same reference counterpart as
+ * pla_stencil7x7_forward.
+ */
+PLA_API int pla_stencil7x7_forward_taps(const void* x, const float* taps, const float* bias, void* y,
+                                        int n, int h, int width,
+                                        int64_t sn, int64_t sh, int64_t sw,
+                                        int dtype, pla_stream_t stream);
+
+/*
  * Depthwise 7x7 convolution (groups = C, stride 1, padding 3):
  *     y[n,c] = stencil(x[n,c]; w[c, 0..48]) + b[c]
  *
@@ -121,6 +137,11 @@ PLA_API int pla_stencil7x7_iterate(const void* x, const void* w, const void* b, 
                            void* scratch, int h, int width, int steps,
                            int dtype, pla_stream_t stream);
 
+/* pla_stencil7x7_iterate with host taps (see pla_stencil7x7_forward_taps). */
+PLA_API int pla_stencil7x7_iterate_taps(const void* x, const float* taps, const float* bias, void* y,
+                                        void* scratch, int h, int width, int steps,
+                                        int dtype, pla_stream_t stream);
+
 /*
  * One Jacobi step of a row band of a larger grid (building block of the
  * row-band multi-GPU iterated stencil; no reference counterpart).
@@ -133,6 +154,11 @@ PLA_API int pla_stencil7x7_iterate(const void* x, const void* w, const void* b, 
 PLA_API int pla_stencil7x7_band_step(const void* in, const void* w, const void* b, void* out,
                              int rows, int width, int row_begin, int row_end,
                              int dtype, pla_stream_t stream);
+
+/* pla_stencil7x7_band_step with host taps (see pla_stencil7x7_forward_taps). */
+PLA_API int pla_stencil7x7_band_step_taps(const void* in, const float* taps, const float* bias, void* out,
+                                          int rows, int width, int row_begin, int row_end,
+                                          int dtype, pla_stream_t stream);
 
 /*
  * Device-side fault word of the current device: bit 0 = an mbarrier wait in a

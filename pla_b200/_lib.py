@@ -15,6 +15,7 @@ _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libpla_b200.so")
 
 PLA_F16, PLA_F32, PLA_F64, PLA_BF16 = 0, 1, 2, 3
+PLA_OK, PLA_ERR_UNSUPPORTED = 0, 2
 PLA_NCHW, PLA_NHWC = 0, 1
 
 DTYPE_CODE = {
@@ -26,14 +27,18 @@ DTYPE_CODE = {
 
 # Every symbol include/pla_b200.h declares, with its ctypes signature.
 _vp, _i32, _i64, _u32p = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.POINTER(ctypes.c_uint)
+_f32p = ctypes.POINTER(ctypes.c_float)
 SIGNATURES = {
     "pla_status_string": ([_i32], ctypes.c_char_p),
     "pla_last_cuda_error": ([], ctypes.c_char_p),
     "pla_version": ([], _i32),
     "pla_stencil7x7_forward": ([_vp, _vp, _vp, _vp, _i32, _i32, _i32, _i64, _i64, _i64, _i32, _vp], _i32),
+    "pla_stencil7x7_forward_taps": ([_vp, _f32p, _f32p, _vp, _i32, _i32, _i32, _i64, _i64, _i64, _i32, _vp], _i32),
     "pla_depthwise7x7_forward": ([_vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _i32, _vp], _i32),
     "pla_stencil7x7_iterate": ([_vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _vp], _i32),
+    "pla_stencil7x7_iterate_taps": ([_vp, _f32p, _f32p, _vp, _vp, _i32, _i32, _i32, _i32, _vp], _i32),
     "pla_stencil7x7_band_step": ([_vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _vp], _i32),
+    "pla_stencil7x7_band_step_taps": ([_vp, _f32p, _f32p, _vp, _i32, _i32, _i32, _i32, _i32, _vp], _i32),
     "pla_read_device_faults": ([_u32p], _i32),
     "pla_clear_device_faults": ([], _i32),
 }
@@ -76,3 +81,38 @@ def stream_ptr(device: torch.device) -> int:
 
 def ptr(t: torch.Tensor | None):
     return None if t is None else t.data_ptr()
+
+
+class HostTaps:
+    """A 7x7 filter (+ optional bias) copied to host fp32 memory for the *_taps entry points.
+
+    Mirrors the reference's weight cache (data/depthwise_conv_7x7_cuda/
+    model_cutlass_autotune_v6.py:507-513, keyed on the parameter's _version
+    and storage): the device->host copy (a stream sync) happens only when the
+    weight or bias tensor changed since the last call.
+    """
+
+    def __init__(self):
+        self._key = None
+        self.taps = (ctypes.c_float * 49)()
+        self.bias = ctypes.c_float(0.0)
+        self.has_bias = False
+
+    @staticmethod
+    def _tkey(t):
+        return None if t is None else (t.data_ptr(), t._version, t.dtype, str(t.device))
+
+    def update(self, weight: torch.Tensor, bias: torch.Tensor | None) -> "HostTaps":
+        key = (self._tkey(weight), self._tkey(bias))
+        if key != self._key:
+            w = weight.detach().reshape(49).float().cpu()
+            for k in range(49):
+                self.taps[k] = float(w[k])
+            self.has_bias = bias is not None
+            if bias is not None:
+                self.bias.value = float(bias.detach().reshape(-1)[0].float().cpu())
+            self._key = key
+        return self
+
+    def args(self):
+        return self.taps, (ctypes.byref(self.bias) if self.has_bias else None)

@@ -14,6 +14,7 @@
 #include "cm_kernel.cuh"
 #include "generic_kernel.cuh"
 #include "pla_common.cuh"
+#include "stack_kernel.cuh"
 #include "tile_kernel.cuh"
 
 namespace pla {
@@ -177,9 +178,10 @@ bool tile_path_ok(const void* x, const void* y, int dtype, int width, long long 
 }
 
 template <typename T>
-int launch_tile(const void* x, const void* w, const void* b, void* y, int dtype, int planes, int C, int in_rows,
-                int width, long long x_row_stride, long long x_plane_stride, int row_begin, int row_end,
-                int in_row_shift, long long y_plane_stride, long long y_row_stride, cudaStream_t stream) {
+int launch_tile(const void* x, const void* w, const void* b, const HostTaps* ht, void* y, int dtype, int planes,
+                int C, int in_rows, int width, long long x_row_stride, long long x_plane_stride, int row_begin,
+                int row_end, int in_row_shift, long long y_plane_stride, long long y_row_stride,
+                cudaStream_t stream) {
   using G = TileGeom<T, kTileR>;
   int st;
   DeviceInfo* d = device_info(&st);
@@ -189,7 +191,8 @@ int launch_tile(const void* x, const void* w, const void* b, void* y, int dtype,
   st = make_tile_map<T, kTileR>(&map, x, dtype, width, in_rows, planes, x_row_stride, x_plane_stride);
   if (st != PLA_OK) return st;
   int per_sm = 1;
-  st = kernel_setup<tile_kernel<T, kTileR>>(kTileThreads, G::SMEM, &per_sm);
+  st = ht ? kernel_setup<tile_kernel<T, kTileR, true>>(kTileThreads, G::SMEM, &per_sm)
+          : kernel_setup<tile_kernel<T, kTileR, false>>(kTileThreads, G::SMEM, &per_sm);
   if (st != PLA_OK) return st;
   TileArgs a;
   a.w = w;
@@ -203,34 +206,53 @@ int launch_tile(const void* x, const void* w, const void* b, void* y, int dtype,
   a.in_row_shift = in_row_shift;
   a.tiles_x = (width + kTileW - 1) / kTileW;
   a.tiles_y = (row_end - row_begin + G::TH - 1) / G::TH;
-  a.total_tiles = static_cast<long long>(planes) * a.tiles_x * a.tiles_y;
+  const long long total = static_cast<long long>(planes) * a.tiles_x * a.tiles_y;
+  if (total > 0x7fffffffll) return PLA_ERR_TOO_LARGE;
+  a.total_tiles = static_cast<int>(total);
+  a.div_tx = make_fastdiv(a.tiles_x);
+  a.div_ty = make_fastdiv(a.tiles_y);
+  a.div_c = make_fastdiv(C);
   a.y_plane_stride = y_plane_stride;
   a.y_row_stride = y_row_stride;
   const long long slots = static_cast<long long>(d->sms) * per_sm;
-  const int grid = static_cast<int>(a.total_tiles < slots ? a.total_tiles : slots);
-  tile_kernel<T, kTileR><<<grid, kTileThreads, G::SMEM, stream>>>(map, a);
+  const int grid = static_cast<int>(total < slots ? total : slots);
+  if (ht) {
+    tile_kernel<T, kTileR, true><<<grid, kTileThreads, G::SMEM, stream>>>(map, a, *ht);
+  } else {
+    HostTaps unused{};
+    tile_kernel<T, kTileR, false><<<grid, kTileThreads, G::SMEM, stream>>>(map, a, unused);
+  }
   PLA_CUDA(cudaGetLastError());
   return PLA_OK;
 }
 
-int launch_tile_dtype(int dtype, const void* x, const void* w, const void* b, void* y, int planes, int C,
-                      int in_rows, int width, long long x_row_stride, long long x_plane_stride, int row_begin,
-                      int row_end, int in_row_shift, long long y_plane_stride, long long y_row_stride,
-                      cudaStream_t stream) {
+int launch_tile_dtype(int dtype, const void* x, const void* w, const void* b, const HostTaps* ht, void* y,
+                      int planes, int C, int in_rows, int width, long long x_row_stride, long long x_plane_stride,
+                      int row_begin, int row_end, int in_row_shift, long long y_plane_stride,
+                      long long y_row_stride, cudaStream_t stream) {
   switch (dtype) {
     case PLA_F32:
-      return launch_tile<float>(x, w, b, y, dtype, planes, C, in_rows, width, x_row_stride, x_plane_stride,
+      return launch_tile<float>(x, w, b, ht, y, dtype, planes, C, in_rows, width, x_row_stride, x_plane_stride,
                                 row_begin, row_end, in_row_shift, y_plane_stride, y_row_stride, stream);
     case PLA_BF16:
-      return launch_tile<__nv_bfloat16>(x, w, b, y, dtype, planes, C, in_rows, width, x_row_stride,
+      return launch_tile<__nv_bfloat16>(x, w, b, ht, y, dtype, planes, C, in_rows, width, x_row_stride,
                                         x_plane_stride, row_begin, row_end, in_row_shift, y_plane_stride,
                                         y_row_stride, stream);
     case PLA_F16:
-      return launch_tile<__half>(x, w, b, y, dtype, planes, C, in_rows, width, x_row_stride, x_plane_stride,
+      return launch_tile<__half>(x, w, b, ht, y, dtype, planes, C, in_rows, width, x_row_stride, x_plane_stride,
                                  row_begin, row_end, in_row_shift, y_plane_stride, y_row_stride, stream);
     default:
       return PLA_ERR_UNSUPPORTED;
   }
+}
+
+// Host taps (fp32) -> kernel-parameter filter.
+HostTaps make_host_taps(const float* taps, const float* bias) {
+  HostTaps h;
+  for (int k = 0; k < kTaps; ++k) h.w[k] = taps[k];
+  h.b = bias ? *bias : 0.f;
+  h.has_b = bias != nullptr;
+  return h;
 }
 
 template <typename T>
@@ -296,7 +318,182 @@ int launch_cm_dtype(int dtype, bool nhwc, const CmArgs& a, cudaStream_t stream) 
   }
 }
 
+// ---- plane-stack kernel (small square planes, NCHW or NHWC) ----------------
+template <typename T>
+int make_nhwc_map(CUtensorMap* map, const void* base, int dtype, int n, int c, int h, int w, int lanes, int s) {
+  PFN_cuTensorMapEncodeTiled_v12000 enc;
+  int st = encoder(&enc);
+  if (st != PLA_OK) return st;
+  const cuuint64_t es = sizeof(T);
+  const cuuint64_t dims[4] = {static_cast<cuuint64_t>(c), static_cast<cuuint64_t>(w), static_cast<cuuint64_t>(h),
+                              static_cast<cuuint64_t>(n)};
+  const cuuint64_t strides[3] = {c * es, static_cast<cuuint64_t>(w) * c * es,
+                                 static_cast<cuuint64_t>(h) * w * c * es};
+  const cuuint32_t box[4] = {static_cast<cuuint32_t>(lanes), static_cast<cuuint32_t>(s),
+                             static_cast<cuuint32_t>(s), 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = enc(map, tmap_dtype(dtype), 4, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    std::snprintf(g_last_cuda_error, sizeof(g_last_cuda_error), "cuTensorMapEncodeTiled (4d) failed (%d)",
+                  static_cast<int>(r));
+    return PLA_ERR_CUDA;
+  }
+  return PLA_OK;
+}
+
+template <typename T, bool NHWC, int S>
+int launch_stack(const void* x, const void* w, const void* b, void* y, int dtype, int n, int c,
+                 cudaStream_t stream) {
+  using G = StackGeom<S>;
+  using M = StackSmem<T, S>;
+  int st;
+  DeviceInfo* d = device_info(&st);
+  if (!d) return st;
+  StackArgs a;
+  a.x = x; a.w = w; a.b = b; a.y = y;
+  a.N = n; a.C = c;
+  a.planes = static_cast<long long>(n) * c;
+  CUtensorMap xmap, ymap;
+  std::memset(&xmap, 0, sizeof(xmap));
+  std::memset(&ymap, 0, sizeof(ymap));
+  long long stages;
+  if (NHWC) {
+    a.cgroups = (c + G::LANES - 1) / G::LANES;
+    stages = static_cast<long long>(n) * a.cgroups;
+    a.full_stages = 0;
+    st = make_nhwc_map<T>(&xmap, x, dtype, n, c, S, S, G::LANES, S);
+    if (st != PLA_OK) return st;
+    st = make_nhwc_map<T>(&ymap, y, dtype, n, c, S, S, G::LANES, S);
+    if (st != PLA_OK) return st;
+  } else {
+    a.cgroups = 1;
+    stages = (a.planes + G::LANES - 1) / G::LANES;
+    a.full_stages = static_cast<int>(a.planes / G::LANES);
+  }
+  if (stages == 0) return PLA_OK;
+  a.stages = static_cast<int>(stages);
+  a.div_c = make_fastdiv(c);
+  a.div_cg = make_fastdiv(a.cgroups);
+  int per_sm;
+  st = kernel_setup<stack_kernel<T, NHWC, S>>(G::THREADS, M::TOTAL, &per_sm);
+  if (st != PLA_OK) return st;
+  const long long slots = static_cast<long long>(d->sms) * per_sm;
+  const int grid = static_cast<int>(stages < slots ? stages : slots);
+  stack_kernel<T, NHWC, S><<<grid, G::THREADS, M::TOTAL, stream>>>(xmap, ymap, a);
+  PLA_CUDA(cudaGetLastError());
+  return PLA_OK;
+}
+
+// Square planes of side 7, 14 or 28 (and, for NHWC, channel rows that are
+// 16-byte multiples so the 4-D TMA map is legal).
+bool stack_path_ok(const void* x, const void* y, int dtype, int layout, long long n, long long c, int h, int w) {
+  if (dtype != PLA_F32 && dtype != PLA_BF16 && dtype != PLA_F16) return false;
+  if (h != w || (h != 7 && h != 14 && h != 28)) return false;
+  if (!aligned(x, 16) || !aligned(y, 16)) return false;
+  if (n * c >= 0x7fffffffll || n >= 0x7fffffffll) return false;
+  if (layout == PLA_NHWC && (c * static_cast<long long>(dtype_size(dtype))) % 16 != 0) return false;
+  // fp32 28x28 stages do not fit in shared memory (2 x 100 KB raw + 100 KB fp32).
+  if (h == 28 && dtype == PLA_F32) return false;
+  return true;
+}
+
+template <typename T, bool NHWC>
+int launch_stack_s(const void* x, const void* w, const void* b, void* y, int dtype, int n, int c, int s,
+                   cudaStream_t stream) {
+  switch (s) {
+    case 7: return launch_stack<T, NHWC, 7>(x, w, b, y, dtype, n, c, stream);
+    case 14: return launch_stack<T, NHWC, 14>(x, w, b, y, dtype, n, c, stream);
+    default: return launch_stack<T, NHWC, 28>(x, w, b, y, dtype, n, c, stream);
+  }
+}
+
+int launch_stack_dtype(int dtype, bool nhwc, const void* x, const void* w, const void* b, void* y, int n, int c,
+                       int s, cudaStream_t stream) {
+  switch (dtype) {
+    case PLA_F32:
+      return nhwc ? launch_stack_s<float, true>(x, w, b, y, dtype, n, c, s, stream)
+                  : launch_stack_s<float, false>(x, w, b, y, dtype, n, c, s, stream);
+    case PLA_BF16:
+      return nhwc ? launch_stack_s<__nv_bfloat16, true>(x, w, b, y, dtype, n, c, s, stream)
+                  : launch_stack_s<__nv_bfloat16, false>(x, w, b, y, dtype, n, c, s, stream);
+    case PLA_F16:
+      return nhwc ? launch_stack_s<__half, true>(x, w, b, y, dtype, n, c, s, stream)
+                  : launch_stack_s<__half, false>(x, w, b, y, dtype, n, c, s, stream);
+    default:
+      return PLA_ERR_UNSUPPORTED;
+  }
+}
+
 bool valid_dtype(int dtype) { return dtype_size(dtype) != 0; }
+
+int stencil_forward_impl(const void* x, const void* w, const void* b, const HostTaps* ht, void* y, int n, int h,
+                         int width, int64_t sn, int64_t sh, int64_t sw, int dtype, pla_stream_t stream) {
+  if (!valid_dtype(dtype)) return PLA_ERR_UNSUPPORTED;
+  if (n < 0 || h < 0 || width < 0) return PLA_ERR_INVALID_ARGUMENT;
+  if (static_cast<long long>(n) * h * width == 0) return PLA_OK;
+  if (!x || (!w && !ht) || !y) return PLA_ERR_INVALID_ARGUMENT;
+  if (n > 65535 * 1024 || h > (1 << 30) || width > (1 << 30)) return PLA_ERR_TOO_LARGE;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const long long plane = static_cast<long long>(h) * width;
+  if (n == 1) sn = plane;  // ignored for a single plane
+  if (sw == 1 && tile_path_ok(x, y, dtype, width, sh, sn, n)) {
+    return launch_tile_dtype(dtype, x, w, b, ht, y, n, 1, h, width, sh, sn, 0, h, 0, plane, width, s);
+  }
+  if (!w) return PLA_ERR_UNSUPPORTED;  // host taps drive the TMA tile path only
+  GenericArgs a;
+  a.x = x; a.w = w; a.b = b; a.y = y;
+  a.N = n; a.C = 1; a.H = h; a.W = width;
+  a.xs_n = sn; a.xs_c = 0; a.xs_h = sh; a.xs_w = sw;
+  a.ys_n = plane; a.ys_c = 0; a.ys_h = width; a.ys_w = 1;
+  a.total = static_cast<long long>(n) * plane;
+  return launch_generic_dtype(dtype, a, s);
+}
+
+int band_step_impl(const void* in, const void* w, const void* b, const HostTaps* ht, void* out, int rows,
+                   int width, int row_begin, int row_end, int dtype, pla_stream_t stream) {
+  if (dtype != PLA_F32 && dtype != PLA_BF16 && dtype != PLA_F16) return PLA_ERR_UNSUPPORTED;
+  if (rows < 0 || width < 0 || row_begin < 0 || row_end < row_begin || row_end > rows)
+    return PLA_ERR_INVALID_ARGUMENT;
+  if (row_end == row_begin || width == 0) return PLA_OK;
+  if (!in || (!w && !ht) || !out) return PLA_ERR_INVALID_ARGUMENT;
+  const size_t es = dtype_size(dtype);
+  const long long band = static_cast<long long>(rows + 6) * width;
+  void* out_rows = static_cast<char*>(out) + 3ll * width * es;
+  if (!tile_path_ok(in, out_rows, dtype, width, width, band, 1)) return PLA_ERR_UNSUPPORTED;
+  return launch_tile_dtype(dtype, in, w, b, ht, out_rows, 1, 1, rows + 6, width, width, band, row_begin, row_end,
+                           3, band, width, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int iterate_impl(const void* x, const void* w, const void* b, const HostTaps* ht, void* y, void* scratch, int h,
+                 int width, int steps, int dtype, pla_stream_t stream) {
+  if (dtype != PLA_F32 && dtype != PLA_BF16 && dtype != PLA_F16) return PLA_ERR_UNSUPPORTED;
+  if (h < 0 || width < 0 || steps < 0) return PLA_ERR_INVALID_ARGUMENT;
+  const long long plane = static_cast<long long>(h) * width;
+  if (plane == 0) return PLA_OK;
+  if (!x || (!w && !ht) || !y || (!scratch && steps > 0)) return PLA_ERR_INVALID_ARGUMENT;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const size_t bytes = static_cast<size_t>(plane) * dtype_size(dtype);
+  if (steps == 0) {
+    if (x != y) PLA_CUDA(cudaMemcpyAsync(y, x, bytes, cudaMemcpyDeviceToDevice, s));
+    return PLA_OK;
+  }
+  if (!tile_path_ok(x, y, dtype, width, width, plane, 1) || !aligned(scratch, 16)) return PLA_ERR_UNSUPPORTED;
+  const void* src = x;
+  if (x == y && (steps & 1)) {
+    // The first step would write into its own input: start from a copy.
+    PLA_CUDA(cudaMemcpyAsync(scratch, x, bytes, cudaMemcpyDeviceToDevice, s));
+    src = scratch;
+  }
+  for (int t = 0; t < steps; ++t) {
+    void* dst = ((steps - t) & 1) ? y : scratch;
+    int st = launch_tile_dtype(dtype, src, w, b, ht, dst, 1, 1, h, width, width, plane, 0, h, 0, plane, width, s);
+    if (st != PLA_OK) return st;
+    src = dst;
+  }
+  return PLA_OK;
+}
 
 }  // namespace
 }  // namespace pla
@@ -324,24 +521,14 @@ int pla_version(void) { return (1 << 16) | 0; }
 
 int pla_stencil7x7_forward(const void* x, const void* w, const void* b, void* y, int n, int h, int width,
                            int64_t sn, int64_t sh, int64_t sw, int dtype, pla_stream_t stream) {
-  if (!valid_dtype(dtype)) return PLA_ERR_UNSUPPORTED;
-  if (n < 0 || h < 0 || width < 0) return PLA_ERR_INVALID_ARGUMENT;
-  if (static_cast<long long>(n) * h * width == 0) return PLA_OK;
-  if (!x || !w || !y) return PLA_ERR_INVALID_ARGUMENT;
-  if (n > 65535 * 1024 || h > (1 << 30) || width > (1 << 30)) return PLA_ERR_TOO_LARGE;
-  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  const long long plane = static_cast<long long>(h) * width;
-  if (n == 1) sn = plane;  // ignored for a single plane
-  if (sw == 1 && tile_path_ok(x, y, dtype, width, sh, sn, n)) {
-    return launch_tile_dtype(dtype, x, w, b, y, n, 1, h, width, sh, sn, 0, h, 0, plane, width, s);
-  }
-  GenericArgs a;
-  a.x = x; a.w = w; a.b = b; a.y = y;
-  a.N = n; a.C = 1; a.H = h; a.W = width;
-  a.xs_n = sn; a.xs_c = 0; a.xs_h = sh; a.xs_w = sw;
-  a.ys_n = plane; a.ys_c = 0; a.ys_h = width; a.ys_w = 1;
-  a.total = static_cast<long long>(n) * plane;
-  return launch_generic_dtype(dtype, a, s);
+  return stencil_forward_impl(x, w, b, nullptr, y, n, h, width, sn, sh, sw, dtype, stream);
+}
+
+int pla_stencil7x7_forward_taps(const void* x, const float* taps, const float* bias, void* y, int n, int h,
+                                int width, int64_t sn, int64_t sh, int64_t sw, int dtype, pla_stream_t stream) {
+  if (!taps) return PLA_ERR_INVALID_ARGUMENT;
+  const HostTaps ht = make_host_taps(taps, bias);
+  return stencil_forward_impl(x, nullptr, nullptr, &ht, y, n, h, width, sn, sh, sw, dtype, stream);
 }
 
 int pla_depthwise7x7_forward(const void* x, const void* w, const void* b, void* y, int n, int c, int h,
@@ -356,10 +543,12 @@ int pla_depthwise7x7_forward(const void* x, const void* w, const void* b, void* 
   const long long plane = static_cast<long long>(h) * width;
   const long long planes = static_cast<long long>(n) * c;
   if (dtype != PLA_F64) {
+    if (stack_path_ok(x, y, dtype, layout, n, c, h, width))
+      return launch_stack_dtype(dtype, layout == PLA_NHWC, x, w, b, y, n, c, h, s);
     if (layout == PLA_NCHW && width >= 64 && planes <= 0x7fffffffll &&
         tile_path_ok(x, y, dtype, width, width, plane, static_cast<int>(planes))) {
-      return launch_tile_dtype(dtype, x, w, b, y, static_cast<int>(planes), c, h, width, width, plane, 0, h, 0,
-                               plane, width, s);
+      return launch_tile_dtype(dtype, x, w, b, nullptr, y, static_cast<int>(planes), c, h, width, width, plane, 0,
+                               h, 0, plane, width, s);
     }
     CmArgs a;
     a.x = x; a.w = w; a.b = b; a.y = y;
@@ -381,46 +570,26 @@ int pla_depthwise7x7_forward(const void* x, const void* w, const void* b, void* 
 
 int pla_stencil7x7_band_step(const void* in, const void* w, const void* b, void* out, int rows, int width,
                              int row_begin, int row_end, int dtype, pla_stream_t stream) {
-  if (dtype != PLA_F32 && dtype != PLA_BF16 && dtype != PLA_F16) return PLA_ERR_UNSUPPORTED;
-  if (rows < 0 || width < 0 || row_begin < 0 || row_end < row_begin || row_end > rows)
-    return PLA_ERR_INVALID_ARGUMENT;
-  if (row_end == row_begin || width == 0) return PLA_OK;
-  if (!in || !w || !out) return PLA_ERR_INVALID_ARGUMENT;
-  const size_t es = dtype_size(dtype);
-  const long long band = static_cast<long long>(rows + 6) * width;
-  void* out_rows = static_cast<char*>(out) + 3ll * width * es;
-  if (!tile_path_ok(in, out_rows, dtype, width, width, band, 1)) return PLA_ERR_UNSUPPORTED;
-  return launch_tile_dtype(dtype, in, w, b, out_rows, 1, 1, rows + 6, width, width, band, row_begin, row_end, 3,
-                           band, width, reinterpret_cast<cudaStream_t>(stream));
+  return band_step_impl(in, w, b, nullptr, out, rows, width, row_begin, row_end, dtype, stream);
+}
+
+int pla_stencil7x7_band_step_taps(const void* in, const float* taps, const float* bias, void* out, int rows,
+                                  int width, int row_begin, int row_end, int dtype, pla_stream_t stream) {
+  if (!taps) return PLA_ERR_INVALID_ARGUMENT;
+  const HostTaps ht = make_host_taps(taps, bias);
+  return band_step_impl(in, nullptr, nullptr, &ht, out, rows, width, row_begin, row_end, dtype, stream);
 }
 
 int pla_stencil7x7_iterate(const void* x, const void* w, const void* b, void* y, void* scratch, int h, int width,
                            int steps, int dtype, pla_stream_t stream) {
-  if (dtype != PLA_F32 && dtype != PLA_BF16 && dtype != PLA_F16) return PLA_ERR_UNSUPPORTED;
-  if (h < 0 || width < 0 || steps < 0) return PLA_ERR_INVALID_ARGUMENT;
-  const long long plane = static_cast<long long>(h) * width;
-  if (plane == 0) return PLA_OK;
-  if (!x || !w || !y || (!scratch && steps > 0)) return PLA_ERR_INVALID_ARGUMENT;
-  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  const size_t bytes = static_cast<size_t>(plane) * dtype_size(dtype);
-  if (steps == 0) {
-    if (x != y) PLA_CUDA(cudaMemcpyAsync(y, x, bytes, cudaMemcpyDeviceToDevice, s));
-    return PLA_OK;
-  }
-  if (!tile_path_ok(x, y, dtype, width, width, plane, 1) || !aligned(scratch, 16)) return PLA_ERR_UNSUPPORTED;
-  const void* src = x;
-  if (x == y && (steps & 1)) {
-    // The first step would write into its own input: start from a copy.
-    PLA_CUDA(cudaMemcpyAsync(scratch, x, bytes, cudaMemcpyDeviceToDevice, s));
-    src = scratch;
-  }
-  for (int t = 0; t < steps; ++t) {
-    void* dst = ((steps - t) & 1) ? y : scratch;
-    int st = launch_tile_dtype(dtype, src, w, b, dst, 1, 1, h, width, width, plane, 0, h, 0, plane, width, s);
-    if (st != PLA_OK) return st;
-    src = dst;
-  }
-  return PLA_OK;
+  return iterate_impl(x, w, b, nullptr, y, scratch, h, width, steps, dtype, stream);
+}
+
+int pla_stencil7x7_iterate_taps(const void* x, const float* taps, const float* bias, void* y, void* scratch, int h,
+                                int width, int steps, int dtype, pla_stream_t stream) {
+  if (!taps) return PLA_ERR_INVALID_ARGUMENT;
+  const HostTaps ht = make_host_taps(taps, bias);
+  return iterate_impl(x, nullptr, nullptr, &ht, y, scratch, h, width, steps, dtype, stream);
 }
 
 int pla_read_device_faults(unsigned int* faults) {

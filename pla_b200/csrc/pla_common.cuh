@@ -27,6 +27,39 @@ constexpr int kHalo = 3;
 // Device fault word (bit 0: an mbarrier wait exceeded its time bound).
 __device__ unsigned int g_device_faults;
 
+// n / d for 0 <= n < 2^31 by one multiply-high and a shift; the divisor is
+// fixed per launch.  m = ceil(2^(31+l) / d) with l = ceil(log2 d) makes the
+// quotient exact for every n < 2^31 (tests/test_host_logic.py checks the
+// same arithmetic exhaustively on edge cases).
+struct FastDiv {
+  unsigned int d, m, s;
+};
+inline FastDiv make_fastdiv(unsigned int d) {
+  FastDiv f;
+  f.d = d;
+  f.m = 0;
+  f.s = 0;
+  if (d <= 1) return f;
+  unsigned int l = 0;
+  while ((1ull << l) < d) ++l;
+  f.m = static_cast<unsigned int>(((1ull << (31 + l)) + d - 1) / d);
+  f.s = l - 1;
+  return f;
+}
+__device__ __forceinline__ int fdiv(int n, const FastDiv& f) {
+  return f.d == 1 ? n : static_cast<int>(__umulhi(static_cast<unsigned int>(n), f.m) >> f.s);
+}
+
+// One filter passed by value (kernel-parameter / constant bank): the FMA
+// instructions read the taps as uniform operands instead of holding 49
+// registers per thread.  Filled on the host from fp32 values (16-bit taps
+// widen exactly).
+struct HostTaps {
+  float w[kTaps];
+  float b;
+  int has_b;
+};
+
 template <typename T> struct AccOf { using type = float; };
 template <> struct AccOf<double> { using type = double; };
 

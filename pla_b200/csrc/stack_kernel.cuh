@@ -1,0 +1,306 @@
+// Plane-stack kernel: depthwise 7x7 on stacks of small square planes
+// (S x S with S in {7, 14, 28}: the ConvNeXt-style shapes of
+// data/depthwise_conv_7x7.py's benchmark configurations), NCHW or NHWC.
+//
+// Work unit ("stage"): LANES = 32 * G planes (NCHW: 32*G consecutive (n, c)
+// planes, contiguous in memory) or LANES channels of one image (NHWC).  Lane
+// l of lane group g owns plane / channel 32 g + l of the stage.
+//
+//  * Load: NCHW stages are one contiguous chunk -> one cp.async.bulk copy;
+//    NHWC stages are one 4-D TMA box (LANES channels x S x S x 1 image).  Both
+//    land raw in a 2-deep shared-memory ring guarded by mbarriers, issued one
+//    stage ahead by thread 0 of a persistent CTA.
+//  * Expand: the raw stage is widened to fp32 into an "x-quad" layout
+//    F[y][x/4][lane][x%4], so that one 128-bit shared load gives a thread 4
+//    consecutive columns of its own plane and a warp's load is 512 contiguous
+//    bytes (bank-conflict free).
+//  * Compute: a thread computes R output rows x S columns of its plane with
+//    the 49 taps of its channel in registers.  Rows and columns that fall on
+//    the zero padding are skipped (compile-time for columns, a warp-uniform
+//    branch for rows): they would add an exact 0, so the fixed (ky, kx) tap
+//    order and hence the bits of every output are unchanged, while 23% (S=14)
+//    to 43% (S=7) of the FMAs of a padded formulation disappear.
+//  * Store: + bias in fp32, one rounding, written back into the stage's raw
+//    buffer (now free) in the source layout and sent out with one bulk copy /
+//    TMA store.
+#pragma once
+
+#include "pla_common.cuh"
+
+namespace pla {
+
+template <int S>
+struct StackGeom {
+  static_assert(S == 7 || S == 14 || S == 28, "plane side");
+  static constexpr int R = (S == 7) ? 7 : 2;           // output rows per thread
+  static constexpr int RG = (S + R - 1) / R;           // row groups per plane
+  static constexpr int G = (S == 7) ? 4 : 1;           // lane groups per CTA
+  static constexpr int WARPS = RG * G;
+  static constexpr int THREADS = 32 * WARPS;
+  static constexpr int LANES = 32 * G;                 // planes / channels per stage
+  static constexpr int Q = (S + 3) / 4;                // x-quads per row
+  static constexpr int F_FLOATS = S * Q * LANES * 4;   // expanded fp32 stage
+  static constexpr int MIN_BLOCKS = (S == 7) ? 4 : (S == 14 ? 2 : 1);
+};
+
+template <typename T, int S>
+struct StackSmem {
+  using G = StackGeom<S>;
+  static constexpr uint32_t RAW = ((G::LANES * S * S * sizeof(T)) + 127u) & ~127u;
+  static constexpr uint32_t F_BYTES = G::F_FLOATS * sizeof(float);
+  static constexpr uint32_t OFF_F = 0;
+  static constexpr uint32_t OFF_RAW = F_BYTES;
+  static constexpr uint32_t OFF_BAR = OFF_RAW + 2 * RAW;
+  static constexpr uint32_t TOTAL = OFF_BAR + 2 * sizeof(uint64_t);
+};
+
+struct StackArgs {
+  const void* x;
+  const void* w;   // [C][49]
+  const void* b;   // [C] or nullptr
+  void* y;
+  int N, C;
+  int stages;          // NCHW: ceil(N*C / LANES); NHWC: N * ceil(C / LANES)
+  int cgroups;         // NHWC: ceil(C / LANES)
+  long long planes;    // NCHW: N * C
+  int full_stages;     // NCHW: stages whose chunk is complete (bulk-copy path)
+  FastDiv div_c, div_cg;
+};
+
+// ---- bulk async copies (non-tensor) and 4-D tensor copies ------------------
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void bulk_store(void* dst, const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(smem_u32(src)),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar, int c, int x, int y,
+                                            int n) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c), "r"(x), "r"(y), "r"(n)
+      : "memory");
+}
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, const void* src, int c, int x, int y, int n) {
+  asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(src)), "r"(c), "r"(x), "r"(y), "r"(n)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read_all() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+__device__ __forceinline__ float raw_to_f(float v) { return v; }
+__device__ __forceinline__ float raw_to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
+__device__ __forceinline__ float raw_to_f(__half v) { return __half2float(v); }
+
+template <typename T, bool NHWC, int S>
+__global__ void __launch_bounds__(StackGeom<S>::THREADS, StackGeom<S>::MIN_BLOCKS)
+    stack_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap ymap,
+                 const StackArgs a) {
+  using G = StackGeom<S>;
+  using M = StackSmem<T, S>;
+  constexpr int R = G::R, Q = G::Q, LANES = G::LANES;
+  extern __shared__ __align__(128) unsigned char smem[];
+  float* F = reinterpret_cast<float*>(smem + M::OFF_F);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + M::OFF_BAR);
+  auto raw = [&](int s) { return reinterpret_cast<T*>(smem + M::OFF_RAW + s * M::RAW); };
+
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int warp = tid >> 5;
+  const int grp = warp / G::RG;        // lane group
+  const int rg = warp % G::RG;         // row group
+  const int ln = grp * 32 + lane;      // lane within the stage
+
+  if (tid == 0) {
+    if (NHWC) {
+      prefetch_tensormap(&xmap);
+      prefetch_tensormap(&ymap);
+    }
+    mbar_init(&bars[0], 1);
+    mbar_init(&bars[1], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  const T* x = static_cast<const T*>(a.x);
+  T* y = static_cast<T*>(a.y);
+  constexpr long long PLANE = static_cast<long long>(S) * S;
+  constexpr uint32_t STAGE_BYTES = LANES * S * S * sizeof(T);
+
+  // Issue the loads of stage k into raw buffer s (thread 0 only).
+  auto issue = [&](int k, int s) {
+    if (NHWC) {
+      const int n = fdiv(k, a.div_cg);
+      const int cg = k - n * a.cgroups;
+      fence_proxy_async_smem();
+      mbar_arrive_expect_tx(&bars[s], STAGE_BYTES);
+      tma_load_4d(raw(s), &xmap, &bars[s], cg * LANES, 0, 0, n);
+    } else if (k < a.full_stages) {
+      fence_proxy_async_smem();
+      mbar_arrive_expect_tx(&bars[s], STAGE_BYTES);
+      bulk_load(raw(s), x + static_cast<long long>(k) * LANES * PLANE, STAGE_BYTES, &bars[s]);
+    }
+  };
+
+  int k = blockIdx.x;
+  if (tid == 0 && k < a.stages) issue(k, 0);
+
+  const T* wbase = static_cast<const T*>(a.w);
+  const T* bbase = static_cast<const T*>(a.b);
+  float wt[kTaps];
+  int cur_c = -1;
+  float bias = 0.f;
+
+  for (int it = 0; k < a.stages; ++it, k += gridDim.x) {
+    const int s = it & 1;
+    const int kn = k + gridDim.x;
+    if (tid == 0 && kn < a.stages) {
+      bulk_wait_read_all();  // raw[s^1] carried the previous stage's output
+      issue(kn, s ^ 1);
+    }
+
+    // ---- this lane's channel and filter --------------------------------
+    int c;
+    bool lane_ok;
+    long long plane = 0;
+    int n_img = 0;
+    if (NHWC) {
+      n_img = fdiv(k, a.div_cg);
+      const int cg = k - n_img * a.cgroups;
+      c = cg * LANES + ln;
+      lane_ok = c < a.C;
+    } else {
+      plane = static_cast<long long>(k) * LANES + ln;
+      lane_ok = plane < a.planes;
+      const int p = static_cast<int>(plane);  // planes < 2^31 (host check)
+      c = p - fdiv(p, a.div_c) * a.C;
+    }
+    const int cw = lane_ok ? c : 0;
+    if (cw != cur_c) {
+      cur_c = cw;
+#pragma unroll
+      for (int t = 0; t < kTaps; ++t) wt[t] = to_acc(wbase[cw * kTaps + t]);
+      bias = bbase ? to_acc(bbase[cw]) : 0.f;
+    }
+
+    // ---- raw stage in shared memory ------------------------------------
+    T* rs = raw(s);
+    const bool partial = !NHWC && k >= a.full_stages;
+    if (partial) {
+      // Tail chunk that a bulk copy cannot move (fewer planes than LANES or a
+      // size that is not a multiple of 16 bytes): plain loads, zero fill.
+      const long long base = static_cast<long long>(k) * LANES * PLANE;
+      const long long left = (a.planes - static_cast<long long>(k) * LANES) * PLANE;
+      for (int i = tid; i < LANES * PLANE; i += G::THREADS) rs[i] = i < left ? x[base + i] : T(0.f);
+      __syncthreads();
+    } else {
+      mbar_wait_bounded(&bars[s], (it >> 1) & 1);
+    }
+
+    // ---- widen to fp32, x-quad layout F[y][q][lane][4] -------------------
+    for (int i = tid; i < S * Q * LANES; i += G::THREADS) {
+      const int l = i % LANES;
+      const int yq = i / LANES;
+      const int yy = yq / Q, q = yq % Q;
+      float4 v;
+      float* vv = reinterpret_cast<float*>(&v);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int xx = 4 * q + j;
+        float f = 0.f;
+        if (xx < S) {
+          const T e = NHWC ? rs[(yy * S + xx) * LANES + l] : rs[l * PLANE + yy * S + xx];
+          f = raw_to_f(e);
+        }
+        vv[j] = f;
+      }
+      reinterpret_cast<float4*>(F)[i] = v;
+    }
+    __syncthreads();
+
+    // ---- R output rows x S columns of plane `ln` -----------------------------
+    float acc[R][S];
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+#pragma unroll
+      for (int o = 0; o < S; ++o) acc[r][o] = 0.f;
+
+    const float4* F4 = reinterpret_cast<const float4*>(F) + ln;
+#pragma unroll
+    for (int ir = 0; ir < R + 6; ++ir) {
+      const int iy = rg * R + ir - kHalo;
+      if (iy < 0 || iy >= S) continue;  // zero-padding row (warp-uniform)
+      float v[4 * Q];
+#pragma unroll
+      for (int q = 0; q < Q; ++q) {
+        const float4 t = F4[(iy * Q + q) * LANES];
+        v[4 * q] = t.x; v[4 * q + 1] = t.y; v[4 * q + 2] = t.z; v[4 * q + 3] = t.w;
+      }
+#pragma unroll
+      for (int kx = 0; kx < 7; ++kx) {
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          const int ky = ir - r;
+          if (ky < 0 || ky >= 7) continue;
+          const float wv = wt[ky * 7 + kx];
+#pragma unroll
+          for (int o = 0; o < S; ++o) {
+            const int ix = o + kx - kHalo;
+            if (ix < 0 || ix >= S) continue;  // zero-padding column (compile time)
+            acc[r][o] = fma_rn(v[ix], wv, acc[r][o]);
+          }
+        }
+      }
+    }
+
+    // ---- + bias, round, stage the output in raw[s] (its input is consumed) ----
+    const bool has_bias = bbase != nullptr;
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const int oy = rg * R + r;
+      if (oy >= S) continue;
+#pragma unroll
+      for (int o = 0; o < S; ++o) {
+        float val = acc[r][o];
+        if (has_bias) val += bias;
+        const T e = from_acc<T>(val);
+        if (NHWC)
+          rs[(oy * S + o) * LANES + ln] = e;
+        else
+          rs[ln * PLANE + oy * S + o] = e;
+      }
+    }
+    fence_proxy_async_smem();
+    __syncthreads();
+
+    if (partial) {
+      const long long base = static_cast<long long>(k) * LANES * PLANE;
+      const long long left = (a.planes - static_cast<long long>(k) * LANES) * PLANE;
+      for (int i = tid; i < LANES * PLANE && i < left; i += G::THREADS) y[base + i] = rs[i];
+    } else if (tid == 0) {
+      if (NHWC) {
+        const int cg = k - n_img * a.cgroups;
+        tma_store_4d(&ymap, rs, cg * LANES, 0, 0, n_img);
+      } else {
+        bulk_store(y + static_cast<long long>(k) * LANES * PLANE, rs, STAGE_BYTES);
+      }
+      bulk_commit();
+    }
+    (void)lane_ok;
+  }
+  if (tid == 0) bulk_wait_all();
+}
+
+}  // namespace pla

@@ -51,14 +51,19 @@ struct TileArgs {
   int row_begin, row_end;   // output rows computed: [row_begin, row_end)
   int in_row_shift;         // input row (tensor-map y) of output row r is r + in_row_shift
   int tiles_x, tiles_y;     // tiles per plane
-  long long total_tiles;    // planes * tiles_y * tiles_x
+  int total_tiles;          // planes * tiles_y * tiles_x (< 2^31, checked on the host)
+  FastDiv div_tx, div_ty, div_c;
   long long y_plane_stride; // elements
   long long y_row_stride;   // elements
 };
 
-template <typename T, int R>
-__global__ void __launch_bounds__(kTileThreads, 4)
-    tile_kernel(const __grid_constant__ CUtensorMap tmap, const TileArgs a) {
+// HOST_TAPS: one filter for every plane, read from the HostTaps parameter;
+// otherwise plane p uses the device filter a.w[(p % C) * 49 ...] held in
+// registers.
+template <typename T, int R, bool HOST_TAPS>
+__global__ void __launch_bounds__(kTileThreads, HOST_TAPS ? 5 : 4)
+    tile_kernel(const __grid_constant__ CUtensorMap tmap, const TileArgs a,
+                const __grid_constant__ HostTaps taps) {
   using G = TileGeom<T, R>;
   extern __shared__ __align__(128) unsigned char smem[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 2 * G::STAGE);
@@ -75,15 +80,15 @@ __global__ void __launch_bounds__(kTileThreads, 4)
   }
   __syncthreads();
 
-  const long long total = a.total_tiles;
-  const long long stride = gridDim.x;
-  long long t = blockIdx.x;
+  const int total = a.total_tiles;
+  const int stride = gridDim.x;
+  int t = blockIdx.x;
 
-  auto issue = [&](long long tile, int stage) {
-    const int tx = static_cast<int>(tile % a.tiles_x);
-    const long long q = tile / a.tiles_x;
-    const int ty = static_cast<int>(q % a.tiles_y);
-    const int plane = static_cast<int>(q / a.tiles_y);
+  auto issue = [&](int tile, int stage) {
+    const int q = fdiv(tile, a.div_tx);
+    const int tx = tile - q * a.tiles_x;
+    const int plane = fdiv(q, a.div_ty);
+    const int ty = q - plane * a.tiles_y;
     const int x0 = tx * kTileW - G::LEFT;
     const int y0 = a.row_begin + ty * G::TH + a.in_row_shift - kHalo;
     fence_proxy_async_smem();
@@ -103,16 +108,18 @@ __global__ void __launch_bounds__(kTileThreads, 4)
     const int stage = it & 1;
     if (tid == 0 && t + stride < total) issue(t + stride, stage ^ 1);
 
-    const int tx = static_cast<int>(t % a.tiles_x);
-    const long long q = t / a.tiles_x;
-    const int ty = static_cast<int>(q % a.tiles_y);
-    const int plane = static_cast<int>(q / a.tiles_y);
-    const int c = plane % a.C;
-    if (c != cur_c) {
-      cur_c = c;
+    const int q = fdiv(t, a.div_tx);
+    const int tx = t - q * a.tiles_x;
+    const int plane = fdiv(q, a.div_ty);
+    const int ty = q - plane * a.tiles_y;
+    if (!HOST_TAPS) {
+      const int c = plane - fdiv(plane, a.div_c) * a.C;
+      if (c != cur_c) {
+        cur_c = c;
 #pragma unroll
-      for (int k = 0; k < kTaps; ++k) wt[k] = to_acc(wt_base[c * kTaps + k]);
-      bias = b_base ? to_acc(b_base[c]) : 0.f;
+        for (int k = 0; k < kTaps; ++k) wt[k] = to_acc(wt_base[c * kTaps + k]);
+        bias = b_base ? to_acc(b_base[c]) : 0.f;
+      }
     }
 
     mbar_wait_bounded(&bars[stage], (it >> 1) & 1);
@@ -136,7 +143,7 @@ __global__ void __launch_bounds__(kTileThreads, 4)
         for (int r = 0; r < R; ++r) {
           const int ky = ir - r;
           if (ky >= 0 && ky < 7) {
-            const float wv = wt[ky * 7 + kx];
+            const float wv = HOST_TAPS ? taps.w[ky * 7 + kx] : wt[ky * 7 + kx];
 #pragma unroll
             for (int j = 0; j < 4; ++j) acc[r][j] = fma_rn(v[j + kx + 1], wv, acc[r][j]);
           }
@@ -148,9 +155,10 @@ __global__ void __launch_bounds__(kTileThreads, 4)
 
     const int ox = tx * kTileW + 4 * lane;
     if (ox < a.W) {
-      T* yp = static_cast<T*>(a.y) + plane * a.y_plane_stride + ox;
+      T* yp = static_cast<T*>(a.y) + static_cast<long long>(plane) * a.y_plane_stride + ox;
       const int oy0 = a.row_begin + ty * G::TH + warp * R;
-      const bool has_bias = b_base != nullptr;
+      const bool has_bias = HOST_TAPS ? taps.has_b != 0 : b_base != nullptr;
+      if (HOST_TAPS) bias = taps.b;
 #pragma unroll
       for (int r = 0; r < R; ++r) {
         const int oy = oy0 + r;
@@ -159,7 +167,7 @@ __global__ void __launch_bounds__(kTileThreads, 4)
           if (has_bias) {
             o0 += bias; o1 += bias; o2 += bias; o3 += bias;
           }
-          store4(yp + oy * a.y_row_stride, o0, o1, o2, o3);
+          store4(yp + static_cast<long long>(oy) * a.y_row_stride, o0, o1, o2, o3);
         }
       }
     }

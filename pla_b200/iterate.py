@@ -27,8 +27,13 @@ from . import _lib
 
 
 def stencil7x7_iterate(x: torch.Tensor, weight: torch.Tensor, steps: int, bias: torch.Tensor | None = None,
-                       out: torch.Tensor | None = None, scratch: torch.Tensor | None = None) -> torch.Tensor:
-    """Apply the 7x7 stencil `steps` times to the CUDA grid x [H, W] (fp32/bf16/fp16)."""
+                       out: torch.Tensor | None = None, scratch: torch.Tensor | None = None,
+                       host_taps: _lib.HostTaps | None = None) -> torch.Tensor:
+    """Apply the 7x7 stencil `steps` times to the CUDA grid x [H, W] (fp32/bf16/fp16).
+
+    The filter is copied to the host once per call (or taken from
+    ``host_taps``) so every step runs the constant-operand kernel.
+    """
     if not isinstance(x, torch.Tensor) or not x.is_cuda:
         raise ValueError("stencil7x7_iterate requires a CUDA input")
     if x.dim() != 2 or not x.is_contiguous():
@@ -44,13 +49,14 @@ def stencil7x7_iterate(x: torch.Tensor, weight: torch.Tensor, steps: int, bias: 
         out = torch.empty_like(x)
     if scratch is None:
         scratch = torch.empty_like(x)
-    weight = weight.detach().contiguous()
-    bias = None if bias is None else bias.detach().contiguous()
+    if host_taps is None:
+        host_taps = _lib.HostTaps().update(weight, bias)
+    taps, hb = host_taps.args()
     with torch.cuda.device(x.device):
-        st = _lib.lib().pla_stencil7x7_iterate(
-            x.data_ptr(), weight.data_ptr(), _lib.ptr(bias), out.data_ptr(), scratch.data_ptr(), H, W, steps,
+        st = _lib.lib().pla_stencil7x7_iterate_taps(
+            x.data_ptr(), taps, hb, out.data_ptr(), scratch.data_ptr(), H, W, steps,
             _lib.DTYPE_CODE[x.dtype], _lib.stream_ptr(x.device))
-    _lib.check(st, "pla_stencil7x7_iterate")
+    _lib.check(st, "pla_stencil7x7_iterate_taps")
     return out
 
 
@@ -73,12 +79,13 @@ StepFn = Callable[[torch.Tensor, torch.Tensor, int, int], None]
 def _cuda_band_step(weight: torch.Tensor, bias: Optional[torch.Tensor]) -> StepFn:
     L = _lib.lib()
     code = _lib.DTYPE_CODE[weight.dtype]
+    taps, hb = _lib.HostTaps().update(weight, bias).args()
 
     def step(src: torch.Tensor, dst: torch.Tensor, row_begin: int, row_end: int) -> None:
         rows, W = src.shape[0] - 6, src.shape[1]
-        st = L.pla_stencil7x7_band_step(src.data_ptr(), weight.data_ptr(), _lib.ptr(bias), dst.data_ptr(), rows,
-                                        W, row_begin, row_end, code, _lib.stream_ptr(src.device))
-        _lib.check(st, "pla_stencil7x7_band_step")
+        st = L.pla_stencil7x7_band_step_taps(src.data_ptr(), taps, hb, dst.data_ptr(), rows, W, row_begin,
+                                             row_end, code, _lib.stream_ptr(src.device))
+        _lib.check(st, "pla_stencil7x7_band_step_taps")
 
     return step
 

@@ -172,6 +172,42 @@ def test_depthwise_configs_full_size(name, shape, dtype, layout, bias, seed):
         torch.testing.assert_close(y.cpu().float(), acc.to(dtype).float(), rtol=tol, atol=tol)
 
 
+@pytest.mark.parametrize("shape,layout,dtype", [
+    ((3, 13, 14, 14), "nchw", torch.bfloat16),   # planes not a multiple of 32: tail stage
+    ((2, 40, 14, 14), "nhwc", torch.bfloat16),   # channels not a multiple of 32: clipped TMA box
+    ((5, 24, 7, 7), "nhwc", torch.float32),      # 7x7 NHWC, 128-channel stages
+    ((3, 50, 7, 7), "nchw", torch.float16),      # 7x7 NCHW, partial 128-plane stage
+    ((2, 64, 28, 28), "nhwc", torch.bfloat16),
+    ((2, 33, 28, 28), "nchw", torch.bfloat16),
+    ((1, 16, 28, 28), "nchw", torch.float32),    # fp32 28x28 falls back to the channel-minor kernel
+    ((2, 33, 14, 14), "nhwc", torch.bfloat16),   # C*2 bytes not a multiple of 16: channel-minor kernel
+    ((2, 8, 12, 12), "nchw", torch.bfloat16),    # non-stack size
+])
+def test_depthwise_stack_shapes(shape, layout, dtype):
+    from pla_b200 import depthwise7x7
+
+    x, w, b = _dw_inputs(11, shape, dtype, True)
+    if layout == "nhwc":
+        x = x.contiguous(memory_format=torch.channels_last)
+    y = depthwise7x7(x.to(DEV), w.to(DEV), b.to(DEV))
+    _assert_equal(y, oracle.depthwise7x7(x, w, b))
+
+
+def test_stencil_host_taps_equals_device_taps():
+    from pla_b200 import _lib, stencil7x7
+
+    g = torch.Generator().manual_seed(9)
+    for dtype in (torch.float32, torch.bfloat16, torch.float16):
+        x = (torch.rand(2, 1, 77, 264, generator=g) * 2 - 1).to(dtype)
+        w = ((torch.rand(1, 1, 7, 7, generator=g) * 2 - 1) / 49).to(dtype)
+        b = ((torch.rand(1, generator=g) * 2 - 1) / 49).to(dtype)
+        xd, wd, bd = x.to(DEV), w.to(DEV), b.to(DEV)
+        y_dev = stencil7x7(xd, wd, bd)
+        y_host = stencil7x7(xd, wd, bd, host_taps=_lib.HostTaps().update(wd, bd))
+        assert torch.equal(y_dev, y_host)
+        _assert_equal(y_host, oracle.stencil7x7(x, w, b))
+
+
 def test_stencil_cfg2_full_size():
     from pla_b200.stencil import ModelNew
 
