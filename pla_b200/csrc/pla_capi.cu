@@ -138,10 +138,9 @@ CUtensorMapDataType tmap_dtype(int dtype) {
 }
 
 // Stack of `planes` planes of `rows` x `width` elements; strides in elements.
-template <typename T, int R>
+template <typename T, typename G>
 int make_tile_map(CUtensorMap* map, const void* x, int dtype, int width, int rows, int planes,
                   long long row_stride, long long plane_stride) {
-  using G = TileGeom<T, R>;
   PFN_cuTensorMapEncodeTiled_v12000 enc;
   int st = encoder(&enc);
   if (st != PLA_OK) return st;
@@ -162,7 +161,10 @@ int make_tile_map(CUtensorMap* map, const void* x, int dtype, int width, int row
   return PLA_OK;
 }
 
-constexpr int kTileR = 8;
+// Tile shapes: wide planes (stencil grids, big depthwise planes) and
+// 33..64-wide planes (one 56 x 64 tile per ConvNeXt stage-1 plane).
+constexpr int kWideR = 8, kWideLX = 32;
+constexpr int kNarrowR = 7, kNarrowLX = 16;
 
 // Can the plane-tile kernel read this stack with TMA?
 bool tile_path_ok(const void* x, const void* y, int dtype, int width, long long row_stride,
@@ -177,22 +179,22 @@ bool tile_path_ok(const void* x, const void* y, int dtype, int width, long long 
   return true;
 }
 
-template <typename T>
+template <typename T, int R, int LX>
 int launch_tile(const void* x, const void* w, const void* b, const HostTaps* ht, void* y, int dtype, int planes,
                 int C, int in_rows, int width, long long x_row_stride, long long x_plane_stride, int row_begin,
                 int row_end, int in_row_shift, long long y_plane_stride, long long y_row_stride,
                 cudaStream_t stream) {
-  using G = TileGeom<T, kTileR>;
+  using G = TileGeom<T, R, LX>;
   int st;
   DeviceInfo* d = device_info(&st);
   if (!d) return st;
   if (row_end <= row_begin || planes == 0 || width == 0) return PLA_OK;
   CUtensorMap map;
-  st = make_tile_map<T, kTileR>(&map, x, dtype, width, in_rows, planes, x_row_stride, x_plane_stride);
+  st = make_tile_map<T, G>(&map, x, dtype, width, in_rows, planes, x_row_stride, x_plane_stride);
   if (st != PLA_OK) return st;
   int per_sm = 1;
-  st = ht ? kernel_setup<tile_kernel<T, kTileR, true>>(kTileThreads, G::SMEM, &per_sm)
-          : kernel_setup<tile_kernel<T, kTileR, false>>(kTileThreads, G::SMEM, &per_sm);
+  st = ht ? kernel_setup<tile_kernel<T, R, LX, true>>(kTileThreads, G::SMEM, &per_sm)
+          : kernel_setup<tile_kernel<T, R, LX, false>>(kTileThreads, G::SMEM, &per_sm);
   if (st != PLA_OK) return st;
   TileArgs a;
   a.w = w;
@@ -204,7 +206,7 @@ int launch_tile(const void* x, const void* w, const void* b, const HostTaps* ht,
   a.row_begin = row_begin;
   a.row_end = row_end;
   a.in_row_shift = in_row_shift;
-  a.tiles_x = (width + kTileW - 1) / kTileW;
+  a.tiles_x = (width + G::TW - 1) / G::TW;
   a.tiles_y = (row_end - row_begin + G::TH - 1) / G::TH;
   const long long total = static_cast<long long>(planes) * a.tiles_x * a.tiles_y;
   if (total > 0x7fffffffll) return PLA_ERR_TOO_LARGE;
@@ -217,30 +219,50 @@ int launch_tile(const void* x, const void* w, const void* b, const HostTaps* ht,
   const long long slots = static_cast<long long>(d->sms) * per_sm;
   const int grid = static_cast<int>(total < slots ? total : slots);
   if (ht) {
-    tile_kernel<T, kTileR, true><<<grid, kTileThreads, G::SMEM, stream>>>(map, a, *ht);
+    tile_kernel<T, R, LX, true><<<grid, kTileThreads, G::SMEM, stream>>>(map, a, *ht);
   } else {
     HostTaps unused{};
-    tile_kernel<T, kTileR, false><<<grid, kTileThreads, G::SMEM, stream>>>(map, a, unused);
+    tile_kernel<T, R, LX, false><<<grid, kTileThreads, G::SMEM, stream>>>(map, a, unused);
   }
   PLA_CUDA(cudaGetLastError());
   return PLA_OK;
 }
 
+template <typename T>
+int launch_tile_shape(bool narrow, const void* x, const void* w, const void* b, const HostTaps* ht, void* y,
+                      int dtype, int planes, int C, int in_rows, int width, long long x_row_stride,
+                      long long x_plane_stride, int row_begin, int row_end, int in_row_shift,
+                      long long y_plane_stride, long long y_row_stride, cudaStream_t stream) {
+  if (narrow)
+    return launch_tile<T, kNarrowR, kNarrowLX>(x, w, b, ht, y, dtype, planes, C, in_rows, width, x_row_stride,
+                                               x_plane_stride, row_begin, row_end, in_row_shift, y_plane_stride,
+                                               y_row_stride, stream);
+  return launch_tile<T, kWideR, kWideLX>(x, w, b, ht, y, dtype, planes, C, in_rows, width, x_row_stride,
+                                         x_plane_stride, row_begin, row_end, in_row_shift, y_plane_stride,
+                                         y_row_stride, stream);
+}
+
+// Narrow tiles only pay off for 33..64-wide planes tall enough to fill them.
+bool use_narrow_tiles(int width, int rows) { return width > 32 && width <= 64 && rows > 28; }
+
 int launch_tile_dtype(int dtype, const void* x, const void* w, const void* b, const HostTaps* ht, void* y,
                       int planes, int C, int in_rows, int width, long long x_row_stride, long long x_plane_stride,
                       int row_begin, int row_end, int in_row_shift, long long y_plane_stride,
                       long long y_row_stride, cudaStream_t stream) {
+  const bool narrow = use_narrow_tiles(width, row_end - row_begin);
   switch (dtype) {
     case PLA_F32:
-      return launch_tile<float>(x, w, b, ht, y, dtype, planes, C, in_rows, width, x_row_stride, x_plane_stride,
-                                row_begin, row_end, in_row_shift, y_plane_stride, y_row_stride, stream);
+      return launch_tile_shape<float>(narrow, x, w, b, ht, y, dtype, planes, C, in_rows, width, x_row_stride,
+                                      x_plane_stride, row_begin, row_end, in_row_shift, y_plane_stride,
+                                      y_row_stride, stream);
     case PLA_BF16:
-      return launch_tile<__nv_bfloat16>(x, w, b, ht, y, dtype, planes, C, in_rows, width, x_row_stride,
-                                        x_plane_stride, row_begin, row_end, in_row_shift, y_plane_stride,
-                                        y_row_stride, stream);
+      return launch_tile_shape<__nv_bfloat16>(narrow, x, w, b, ht, y, dtype, planes, C, in_rows, width,
+                                              x_row_stride, x_plane_stride, row_begin, row_end, in_row_shift,
+                                              y_plane_stride, y_row_stride, stream);
     case PLA_F16:
-      return launch_tile<__half>(x, w, b, ht, y, dtype, planes, C, in_rows, width, x_row_stride, x_plane_stride,
-                                 row_begin, row_end, in_row_shift, y_plane_stride, y_row_stride, stream);
+      return launch_tile_shape<__half>(narrow, x, w, b, ht, y, dtype, planes, C, in_rows, width, x_row_stride,
+                                       x_plane_stride, row_begin, row_end, in_row_shift, y_plane_stride,
+                                       y_row_stride, stream);
     default:
       return PLA_ERR_UNSUPPORTED;
   }
@@ -545,7 +567,7 @@ int pla_depthwise7x7_forward(const void* x, const void* w, const void* b, void* 
   if (dtype != PLA_F64) {
     if (stack_path_ok(x, y, dtype, layout, n, c, h, width))
       return launch_stack_dtype(dtype, layout == PLA_NHWC, x, w, b, y, n, c, h, s);
-    if (layout == PLA_NCHW && width >= 64 && planes <= 0x7fffffffll &&
+    if (layout == PLA_NCHW && (width >= 64 || use_narrow_tiles(width, h)) && planes <= 0x7fffffffll &&
         tile_path_ok(x, y, dtype, width, width, plane, static_cast<int>(planes))) {
       return launch_tile_dtype(dtype, x, w, b, nullptr, y, static_cast<int>(planes), c, h, width, width, plane, 0,
                                h, 0, plane, width, s);

@@ -10,7 +10,7 @@
 //    (cp.async.bulk.tensor, no multicast) into a 2-stage shared-memory ring
 //    guarded by mbarriers, so the next tile streams in while this one is
 //    computed; TMA's out-of-bounds zero fill supplies the zero padding;
-//  * 4 warps x 32 lanes; a thread owns R rows x 4 columns of outputs, loads
+//  * 4 warps; a thread owns R rows x 4 columns of outputs, loads
 //    each input row of its window once with three 128-bit (fp32) or 64-bit
 //    (16-bit types) shared loads and applies it to every output row it
 //    touches (the 7-wide window is reused across the 4 columns in registers);
@@ -23,17 +23,22 @@
 namespace pla {
 
 constexpr int kTileThreads = 128;
-constexpr int kTileW = 128;  // output columns per tile (32 lanes x 4)
 
+// A warp is (32 / LX) row groups x LX column groups; a thread owns R rows x
+// 4 columns, so a tile is TH = 4 warps x (32 / LX) x R rows by TW = 4 LX
+// columns.  (R, LX) = (8, 32) gives the 32 x 128 tiles of wide planes,
+// (7, 16) one 56 x 64 tile per 56-wide plane.
 // The TMA box starts LEFT columns left of the tile: LEFT * sizeof(T) == 16 B
 // keeps the innermost TMA coordinate 16-byte aligned (a hard TMA rule), and
-// LEFT >= 3 covers the halo.  The box is LEFT + 128 + LEFT wide.
-template <typename T, int R>
+// LEFT >= 3 covers the halo.  The box is LEFT + TW + LEFT wide.
+template <typename T, int R, int LX>
 struct TileGeom {
-  static constexpr int TH = 4 * R;           // output rows per tile
+  static_assert(LX == 32 || LX == 16, "column groups per warp");
+  static constexpr int TW = 4 * LX;                     // output columns per tile
+  static constexpr int TH = (kTileThreads / 32) * (32 / LX) * R;  // output rows per tile
   static constexpr int ROWS = TH + 6;        // input rows per tile (3-row halo)
   static constexpr int LEFT = 16 / sizeof(T);
-  static constexpr int PITCH = kTileW + 2 * LEFT;
+  static constexpr int PITCH = TW + 2 * LEFT;
   static_assert(LEFT >= 4 && (LEFT * sizeof(T)) % 16 == 0, "TMA x must stay 16-byte aligned");
   static_assert((PITCH * sizeof(T)) % 16 == 0, "TMA box inner extent must be a multiple of 16 B");
   static constexpr uint32_t BYTES = ROWS * PITCH * sizeof(T);
@@ -60,17 +65,18 @@ struct TileArgs {
 // HOST_TAPS: one filter for every plane, read from the HostTaps parameter;
 // otherwise plane p uses the device filter a.w[(p % C) * 49 ...] held in
 // registers.
-template <typename T, int R, bool HOST_TAPS>
+template <typename T, int R, int LX, bool HOST_TAPS>
 __global__ void __launch_bounds__(kTileThreads, HOST_TAPS ? 5 : 4)
     tile_kernel(const __grid_constant__ CUtensorMap tmap, const TileArgs a,
                 const __grid_constant__ HostTaps taps) {
-  using G = TileGeom<T, R>;
+  using G = TileGeom<T, R, LX>;
   extern __shared__ __align__(128) unsigned char smem[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 2 * G::STAGE);
 
   const int tid = threadIdx.x;
   const int lane = tid & 31;
-  const int warp = tid >> 5;
+  const int rgrp = (tid >> 5) * (32 / LX) + lane / LX;  // row group within the tile
+  const int cgrp = lane % LX;                           // column group within the tile
 
   if (tid == 0) {
     prefetch_tensormap(&tmap);
@@ -89,7 +95,7 @@ __global__ void __launch_bounds__(kTileThreads, HOST_TAPS ? 5 : 4)
     const int tx = tile - q * a.tiles_x;
     const int plane = fdiv(q, a.div_ty);
     const int ty = q - plane * a.tiles_y;
-    const int x0 = tx * kTileW - G::LEFT;
+    const int x0 = tx * G::TW - G::LEFT;
     const int y0 = a.row_begin + ty * G::TH + a.in_row_shift - kHalo;
     fence_proxy_async_smem();
     mbar_arrive_expect_tx(&bars[stage], G::BYTES);
@@ -125,7 +131,7 @@ __global__ void __launch_bounds__(kTileThreads, HOST_TAPS ? 5 : 4)
     mbar_wait_bounded(&bars[stage], (it >> 1) & 1);
 
     // v[k] below is input column ox - 4 + k (ox = this thread's first output column).
-    const T* s = reinterpret_cast<const T*>(smem + stage * G::STAGE) + (warp * R) * G::PITCH + 4 * lane +
+    const T* s = reinterpret_cast<const T*>(smem + stage * G::STAGE) + (rgrp * R) * G::PITCH + 4 * cgrp +
                  (G::LEFT - 4);
     float acc[R][4];
 #pragma unroll
@@ -153,10 +159,10 @@ __global__ void __launch_bounds__(kTileThreads, HOST_TAPS ? 5 : 4)
     // Every thread is done with this stage before it is refilled.
     __syncthreads();
 
-    const int ox = tx * kTileW + 4 * lane;
+    const int ox = tx * G::TW + 4 * cgrp;
     if (ox < a.W) {
       T* yp = static_cast<T*>(a.y) + static_cast<long long>(plane) * a.y_plane_stride + ox;
-      const int oy0 = a.row_begin + ty * G::TH + warp * R;
+      const int oy0 = a.row_begin + ty * G::TH + rgrp * R;
       const bool has_bias = HOST_TAPS ? taps.has_b != 0 : b_base != nullptr;
       if (HOST_TAPS) bias = taps.b;
 #pragma unroll

@@ -1,0 +1,106 @@
+"""Host-side logic that needs no GPU: the kernels' division-free index
+decode, row-band partitioning, and the multi-rank halo exchange of the
+iterated stencil on gloo CPU ranks (the band step computed by the oracle)."""
+import os
+import random
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from oracle import oracle
+
+
+# ---- FastDiv (pla_b200/csrc/pla_common.cuh) restated with the same integers
+def _make_fastdiv(d):
+    if d <= 1:
+        return d, 0, 0
+    l = (d - 1).bit_length()  # ceil(log2 d)
+    m = ((1 << (31 + l)) + d - 1) // d
+    assert m < (1 << 32)
+    return d, m, l - 1
+
+
+def _fdiv(n, f):
+    d, m, s = f
+    return n if d == 1 else ((n * m) >> 32) >> s
+
+
+def test_fastdiv_exact_for_all_int31_dividends():
+    rng = random.Random(0)
+    divisors = list(range(1, 2049)) + [rng.randrange(2, 2 ** 31) for _ in range(2000)] + [2 ** 31 - 1, 2 ** 30,
+                                                                                         2 ** 30 + 1, 3 ** 19]
+    for d in divisors:
+        f = _make_fastdiv(d)
+        for n in [0, 1, d - 1, d, d + 1, 2 * d - 1, 2 ** 31 - 1, 2 ** 31 - 2, max(0, 2 ** 31 - d)] + \
+                 [rng.randrange(0, 2 ** 31) for _ in range(64)]:
+            if 0 <= n < 2 ** 31:
+                assert _fdiv(n, f) == n // d, (n, d)
+
+
+# ---- band partition -----------------------------------------------------------
+def test_band_rows_partition():
+    from pla_b200.iterate import band_rows
+
+    for H in (1, 7, 32, 100, 32768):
+        for world in (1, 2, 3, 4, 8):
+            if H < world:
+                continue
+            bands = [band_rows(H, world, r) for r in range(world)]
+            assert bands[0][0] == 0 and bands[-1][1] == H
+            for (a0, a1), (b0, b1) in zip(bands, bands[1:]):
+                assert a1 == b0
+            sizes = [b - a for a, b in bands]
+            assert max(sizes) - min(sizes) <= 1
+    with pytest.raises(ValueError):
+        band_rows(10, 0, 0)
+
+
+# ---- multi-rank halo exchange on gloo CPU ranks ------------------------------
+def _oracle_band_step(w):
+    def step(src, dst, rb, re):
+        # band row r <-> buffer row r + 3; output rows need buffer rows r .. r+6
+        dst[rb + 3:re + 3] = oracle.stencil7x7_rows(src, w, rb + 3, re + 3)
+    return step
+
+
+def _rank_main(rank, world, port, H, W, steps, out_q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from pla_b200.iterate import BandedStencil
+
+        g = torch.Generator().manual_seed(4)
+        x = torch.rand(H, W, generator=g) * 2 - 1
+        w = torch.rand(7, 7, generator=g) * 2 - 1
+        w = w / w.sum()
+        bs = BandedStencil(H, W, w, device=torch.device("cpu"), step_fn=_oracle_band_step(w))
+        bs.load(x)
+        bs.run(steps)
+        full = bs.gather()
+        if rank == 0:
+            out_q.put(full)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,H,W,steps", [(2, 40, 24, 5), (3, 31, 16, 4), (4, 48, 20, 3)])
+def test_banded_iterate_gloo_matches_single_domain(world, H, W, steps):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29500 + random.Random(world * 1000 + H).randrange(0, 5000)
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, H, W, steps, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    full = q.get(timeout=120)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    g = torch.Generator().manual_seed(4)
+    x = torch.rand(H, W, generator=g) * 2 - 1
+    w = torch.rand(7, 7, generator=g) * 2 - 1
+    w = w / w.sum()
+    ref = oracle.stencil7x7_iterate(x, w, steps)
+    assert torch.equal(full, ref)
