@@ -69,7 +69,8 @@ enum pla_status {
 /* Human-readable text for a status code (static storage, never NULL). */
 PLA_API const char* pla_status_string(int status);
 
-/* The last CUDA error text seen by this thread inside the library. */
+/* Detail text of the last failure seen by this thread inside the library
+ * (CUDA error strings, size limits). */
 PLA_API const char* pla_last_cuda_error(void);
 
 /* Library ABI version: (major << 16) | minor. */
@@ -136,6 +137,33 @@ PLA_API int pla_depthwise7x7_forward(const void* x, const void* w, const void* b
 PLA_API int pla_stencil7x7_iterate(const void* x, const void* w, const void* b, void* y,
                            void* scratch, int h, int width, int steps,
                            int dtype, pla_stream_t stream);
+
+/*
+ * pla_stencil7x7_iterate without a caller scratch buffer, for callers that
+ * cannot allocate device memory: a plugin running inside a host framework
+ * that owns every device allocation, a fixed-budget embedded runtime, or a
+ * real-time loop that cannot afford cudaMalloc's implicit synchronisation.
+ * This entry point has no counterpart in the reference.
+ *
+ * The second ping-pong plane is a 16 MiB static device array inside this
+ * library (PLA_NOALLOC_SCRATCH_BYTES), held by every GPU that loads the
+ * library until the process exits.  Grids larger than that (h * width *
+ * element size > 16 MiB, e.g. more than 2048 x 2048 fp32) return
+ * PLA_ERR_TOO_LARGE with the sizes in pla_last_cuda_error().  Nothing is
+ * allocated: no cudaMalloc/cudaFree or allocating library call.
+ *
+ * The first call on a device looks up the array's device address
+ * (cudaGetSymbolAddress) with that device current; make that first call
+ * before any stream capture.  All calls on a device share the one array and
+ * leave the last call's data in it (no call needs it cleared: every step
+ * overwrites the whole plane before reading it), so calls that overlap on
+ * the GPU (concurrent streams) race on it; serialise them.
+ * Arguments and results are those of pla_stencil7x7_iterate.
+ */
+#define PLA_NOALLOC_SCRATCH_BYTES (16u << 20)
+PLA_API int pla_stencil7x7_iterate_noalloc(const void* x, const void* w, const void* b, void* y,
+                                           int h, int width, int steps,
+                                           int dtype, pla_stream_t stream);
 
 /* pla_stencil7x7_iterate with host taps (see pla_stencil7x7_forward_taps). */
 PLA_API int pla_stencil7x7_iterate_taps(const void* x, const float* taps, const float* bias, void* y,

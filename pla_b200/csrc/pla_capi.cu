@@ -517,6 +517,36 @@ int iterate_impl(const void* x, const void* w, const void* b, const HostTaps* ht
   return PLA_OK;
 }
 
+// ---- allocation-free iterate: file-scope scratch ---------------------------
+// The ping-pong plane of pla_stencil7x7_iterate_noalloc lives here instead of
+// in a caller buffer.  Every GPU that loads this library holds these 16 MiB
+// until the process exits; all calls on a device share them.
+constexpr size_t kNoAllocScratchBytes = size_t(16) << 20;
+static_assert(kNoAllocScratchBytes == PLA_NOALLOC_SCRATCH_BYTES, "header and library agree on the limit");
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+struct NoAllocScratch {
+  std::once_flag once;
+  cudaError_t err = cudaSuccess;
+  void* ptr = nullptr;
+};
+NoAllocScratch g_noalloc[kMaxDevices];
+
+// Device address of g_noalloc_scratch on the current device.  The host-side
+// name of the array is only a stand-in for the symbol, so the address must
+// come from cudaGetSymbolAddress, looked up once per device with that device
+// current (on the first call made on that device).
+int noalloc_scratch(void** out) {
+  int dev;
+  int st = current_device(&dev);
+  if (st != PLA_OK) return st;
+  NoAllocScratch& s = g_noalloc[dev];
+  std::call_once(s.once, [&]() { s.err = cudaGetSymbolAddress(&s.ptr, g_noalloc_scratch); });
+  if (s.err != cudaSuccess) return cuda_fail(s.err, "cudaGetSymbolAddress(g_noalloc_scratch)");
+  *out = s.ptr;
+  return PLA_OK;
+}
+
 }  // namespace
 }  // namespace pla
 
@@ -612,6 +642,26 @@ int pla_stencil7x7_iterate_taps(const void* x, const float* taps, const float* b
   if (!taps) return PLA_ERR_INVALID_ARGUMENT;
   const HostTaps ht = make_host_taps(taps, bias);
   return iterate_impl(x, nullptr, nullptr, &ht, y, scratch, h, width, steps, dtype, stream);
+}
+
+int pla_stencil7x7_iterate_noalloc(const void* x, const void* w, const void* b, void* y, int h, int width,
+                                   int steps, int dtype, pla_stream_t stream) {
+  if (dtype != PLA_F32 && dtype != PLA_BF16 && dtype != PLA_F16) return PLA_ERR_UNSUPPORTED;
+  if (h < 0 || width < 0 || steps < 0) return PLA_ERR_INVALID_ARGUMENT;
+  const unsigned long long bytes =
+      static_cast<unsigned long long>(h) * static_cast<unsigned long long>(width) * dtype_size(dtype);
+  if (bytes > kNoAllocScratchBytes) {
+    std::snprintf(g_last_cuda_error, sizeof(g_last_cuda_error),
+                  "pla_stencil7x7_iterate_noalloc: a %d x %d grid needs %llu scratch bytes, the static "
+                  "scratch holds %llu",
+                  h, width, bytes, static_cast<unsigned long long>(kNoAllocScratchBytes));
+    return PLA_ERR_TOO_LARGE;
+  }
+  if (bytes == 0) return PLA_OK;
+  void* scratch = nullptr;
+  const int st = noalloc_scratch(&scratch);
+  if (st != PLA_OK) return st;
+  return iterate_impl(x, w, b, nullptr, y, scratch, h, width, steps, dtype, stream);
 }
 
 int pla_read_device_faults(unsigned int* faults) {
