@@ -396,8 +396,16 @@ int launch_stack(const void* x, const void* w, const void* b, void* y, int dtype
   }
   if (stages == 0) return PLA_OK;
   a.stages = static_cast<int>(stages);
+  if (NHWC) {
+    a.cg_major = 1;
+  } else {
+    // NCHW stages hold whole channel groups only when LANES divides C.
+    a.cg_major = (c % G::LANES == 0) ? 1 : 0;
+    if (a.cg_major) a.cgroups = c / G::LANES;
+  }
   a.div_c = make_fastdiv(c);
   a.div_cg = make_fastdiv(a.cgroups);
+  a.div_n = make_fastdiv(n);
   int per_sm;
   st = kernel_setup<stack_kernel<T, NHWC, S>>(G::THREADS, M::TOTAL, &per_sm);
   if (st != PLA_OK) return st;

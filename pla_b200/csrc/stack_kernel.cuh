@@ -64,8 +64,22 @@ struct StackArgs {
   int cgroups;         // NHWC: ceil(C / LANES)
   long long planes;    // NCHW: N * C
   int full_stages;     // NCHW: stages whose chunk is complete (bulk-copy path)
-  FastDiv div_c, div_cg;
+  int cg_major;        // 1: visit stages channel-group-major (see stage_of)
+  FastDiv div_c, div_cg, div_n;
 };
+
+// CTAs own contiguous ranges of "virtual" stages.  With cg_major, virtual
+// stage v is (channel group v / N, image v % N), so consecutive stages of a
+// CTA reuse the same 32 (or 128) filters, which then stay in registers; the
+// stage index k (the memory order) is n * cgroups + cg.  This needs every
+// stage to hold whole channel groups: always true for NHWC, and for NCHW when
+// C is a multiple of LANES.
+__device__ __forceinline__ int stage_of(int v, const StackArgs& a) {
+  if (!a.cg_major) return v;
+  const int cg = fdiv(v, a.div_n);
+  const int n = v - cg * a.N;
+  return n * a.cgroups + cg;
+}
 
 // ---- bulk async copies (non-tensor) and 4-D tensor copies ------------------
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
@@ -154,8 +168,10 @@ __global__ void __launch_bounds__(StackGeom<S>::THREADS, StackGeom<S>::MIN_BLOCK
     }
   };
 
-  int k = blockIdx.x;
-  if (tid == 0 && k < a.stages) issue(k, 0);
+  // Balanced contiguous range of virtual stages for this CTA.
+  const int v_begin = static_cast<int>((static_cast<long long>(a.stages) * blockIdx.x) / gridDim.x);
+  const int v_end = static_cast<int>((static_cast<long long>(a.stages) * (blockIdx.x + 1)) / gridDim.x);
+  if (tid == 0 && v_begin < v_end) issue(stage_of(v_begin, a), 0);
 
   const T* wbase = static_cast<const T*>(a.w);
   const T* bbase = static_cast<const T*>(a.b);
@@ -163,12 +179,12 @@ __global__ void __launch_bounds__(StackGeom<S>::THREADS, StackGeom<S>::MIN_BLOCK
   int cur_c = -1;
   float bias = 0.f;
 
-  for (int it = 0; k < a.stages; ++it, k += gridDim.x) {
+  for (int v = v_begin, it = 0; v < v_end; ++v, ++it) {
     const int s = it & 1;
-    const int kn = k + gridDim.x;
-    if (tid == 0 && kn < a.stages) {
+    const int k = stage_of(v, a);
+    if (tid == 0 && v + 1 < v_end) {
       bulk_wait_read_all();  // raw[s^1] carried the previous stage's output
-      issue(kn, s ^ 1);
+      issue(stage_of(v + 1, a), s ^ 1);
     }
 
     // ---- this lane's channel and filter --------------------------------

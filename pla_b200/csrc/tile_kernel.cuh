@@ -133,12 +133,10 @@ __global__ void __launch_bounds__(kTileThreads, HOST_TAPS ? 5 : 4)
     // v[k] below is input column ox - 4 + k (ox = this thread's first output column).
     const T* s = reinterpret_cast<const T*>(smem + stage * G::STAGE) + (rgrp * R) * G::PITCH + 4 * cgrp +
                  (G::LEFT - 4);
+    // The first tap of every output (ky = kx = 0, reached at ir == r) starts
+    // its accumulator with a plain product: RN(x * w) == fma(x, w, +0) except
+    // for the sign of an exact zero, which no later "+" can tell apart.
     float acc[R][4];
-#pragma unroll
-    for (int r = 0; r < R; ++r)
-#pragma unroll
-      for (int j = 0; j < 4; ++j) acc[r][j] = 0.f;
-
 #pragma unroll
     for (int ir = 0; ir < R + 6; ++ir) {
       float v[12];
@@ -151,7 +149,12 @@ __global__ void __launch_bounds__(kTileThreads, HOST_TAPS ? 5 : 4)
           if (ky >= 0 && ky < 7) {
             const float wv = HOST_TAPS ? taps.w[ky * 7 + kx] : wt[ky * 7 + kx];
 #pragma unroll
-            for (int j = 0; j < 4; ++j) acc[r][j] = fma_rn(v[j + kx + 1], wv, acc[r][j]);
+            for (int j = 0; j < 4; ++j) {
+              if (ky == 0 && kx == 0)
+                acc[r][j] = __fmul_rn(v[j + kx + 1], wv);
+              else
+                acc[r][j] = fma_rn(v[j + kx + 1], wv, acc[r][j]);
+            }
           }
         }
       }
@@ -160,22 +163,26 @@ __global__ void __launch_bounds__(kTileThreads, HOST_TAPS ? 5 : 4)
     __syncthreads();
 
     const int ox = tx * G::TW + 4 * cgrp;
-    if (ox < a.W) {
-      T* yp = static_cast<T*>(a.y) + static_cast<long long>(plane) * a.y_plane_stride + ox;
-      const int oy0 = a.row_begin + ty * G::TH + rgrp * R;
-      const bool has_bias = HOST_TAPS ? taps.has_b != 0 : b_base != nullptr;
-      if (HOST_TAPS) bias = taps.b;
+    const bool has_bias = HOST_TAPS ? taps.has_b != 0 : b_base != nullptr;
+    if (HOST_TAPS) bias = taps.b;
+    if (has_bias) {
 #pragma unroll
-      for (int r = 0; r < R; ++r) {
-        const int oy = oy0 + r;
-        if (oy < a.row_end) {
-          float o0 = acc[r][0], o1 = acc[r][1], o2 = acc[r][2], o3 = acc[r][3];
-          if (has_bias) {
-            o0 += bias; o1 += bias; o2 += bias; o3 += bias;
-          }
-          store4(yp + static_cast<long long>(oy) * a.y_row_stride, o0, o1, o2, o3);
-        }
-      }
+      for (int r = 0; r < R; ++r)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[r][j] += bias;
+    }
+    const int oy0 = a.row_begin + ty * G::TH + rgrp * R;
+    T* yp = static_cast<T*>(a.y) + static_cast<long long>(plane) * a.y_plane_stride +
+            static_cast<long long>(oy0) * a.y_row_stride + ox;
+    // Whole tile inside the output (the common case): no per-row tests.
+    const bool interior = (tx + 1) * G::TW <= a.W && a.row_begin + (ty + 1) * G::TH <= a.row_end;
+    if (interior) {
+#pragma unroll
+      for (int r = 0; r < R; ++r) store4(yp + r * a.y_row_stride, acc[r][0], acc[r][1], acc[r][2], acc[r][3]);
+    } else if (ox < a.W) {
+#pragma unroll
+      for (int r = 0; r < R; ++r)
+        if (oy0 + r < a.row_end) store4(yp + r * a.y_row_stride, acc[r][0], acc[r][1], acc[r][2], acc[r][3]);
     }
   }
 }
