@@ -1,0 +1,70 @@
+"""Multi-GPU parity: the row-band iterated stencil over NCCL (one process per
+GPU) must equal the single-GPU iteration bit for bit.  Needs >= 2 GPUs."""
+import os
+import random
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _inputs(H, W):
+    g = torch.Generator().manual_seed(4)
+    x = torch.rand(H, W, generator=g) * 2 - 1
+    w = torch.rand(7, 7, generator=g) * 2 - 1
+    return x, w / w.sum()
+
+
+def _rank(rank, world, port, H, W, steps, q):
+    import datetime
+
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                            timeout=datetime.timedelta(seconds=60))
+    try:
+        from pla_b200 import BandedStencil
+
+        x, w = _inputs(H, W)
+        bs = BandedStencil(H, W, w.to(dev), device=dev)
+        bs.load(x.to(dev))
+        bs.run(steps)
+        full = bs.gather()
+        torch.cuda.synchronize()
+        if rank == 0:
+            q.put(full.cpu())
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("world,H,W,steps", [(2, 1000, 768, 9), (2, 64, 256, 5)])
+def test_banded_nccl_equals_single_gpu(world, H, W, steps):
+    from pla_b200 import stencil7x7_iterate
+
+    x, w = _inputs(H, W)
+    ref = stencil7x7_iterate(x.cuda(), w.cuda(), steps).cpu()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank, args=(r, world, port, H, W, steps, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = q.get(timeout=180)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    assert torch.equal(got, ref)
