@@ -496,11 +496,18 @@ class IterateCfg5:
     def step(self, i):
         self.bs.step()
 
+    def close(self):
+        self.bs.check_faults()
+        self.bs.close()
+
     def config(self):
         return {"workload": self.name, "shape": [self.H, self.W], "seed": 4, "x": "U(-1,1)",
                 "w": "U(-1,1) normalised to sum 1", "bias": False,
                 "l2": "4 GiB grid per buffer >> 126 MB L2",
-                "parallelism": "row bands, 3-row halo exchange per step (NCCL send/recv, side stream, "
+                "parallelism": "row bands, 3-row halo exchange per step fused into the step kernel "
+                               "(edge tiles first, rows stored into the neighbours' halos over NVLink via "
+                               "CUDA IPC, flag handshake; no collective call)" if self.bs.mode == "p2p" else
+                               "row bands, 3-row halo exchange per step (NCCL send/recv on a side stream, "
                                "overlapped with interior rows)"}
 
     def e2e_setup(self):
@@ -711,6 +718,8 @@ def main():
             "wall_s_timed_region": t_wall,
         }
         print(json.dumps(line), flush=True)
+    if hasattr(wl, "close"):
+        wl.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

@@ -189,8 +189,38 @@ PLA_API int pla_stencil7x7_band_step_taps(const void* in, const float* taps, con
                                           int dtype, pla_stream_t stream);
 
 /*
+ * One band step fused with the halo exchange over peer memory (NVLink), the
+ * row-band multi-GPU iterated stencil without a separate collective (no
+ * reference counterpart).  Band buffers as in pla_stencil7x7_band_step; the
+ * step computes every band row (rows >= 64) with the host taps, and
+ *  - before reading its halo, waits (bounded, ~2 s, then fault bit 1) until
+ *    flags[0] >= step (neighbour above delivered) / flags[1] >= step (below);
+ *  - stores its first 3 band rows into up_out rows up_rows+3..up_rows+5 and
+ *    its last 3 into down_out rows 0..2 (the neighbours' `out` buffers, peer
+ *    pointers from pla_ipc_import), then raises up_flags[1] / down_flags[0]
+ *    (the neighbours' flags) to step+1.
+ * up_out/down_out NULL = grid edge (zero halo kept).  flags[2] and counters[2]
+ * are this GPU's zero-initialised words; steps must be launched 0, 1, 2, ...
+ * on every rank.  Ranks are separate GPUs (never two on one device).
+ */
+PLA_API int pla_stencil7x7_band_step_halo(const void* in, const float* taps, const float* bias, void* out,
+                                          int rows, int width, int dtype,
+                                          void* up_out, int up_rows, void* down_out,
+                                          unsigned int* flags, unsigned int* up_flags,
+                                          unsigned int* down_flags, unsigned int* counters,
+                                          unsigned int step, pla_stream_t stream);
+
+/* CUDA IPC: export a device pointer as (64-byte handle of its allocation,
+ * byte offset), import it in another process (peer access enabled lazily),
+ * close an imported pointer. */
+PLA_API int pla_ipc_export(const void* ptr, void* handle, uint64_t* offset);
+PLA_API int pla_ipc_import(const void* handle, uint64_t offset, void** ptr);
+PLA_API int pla_ipc_close(void* ptr, uint64_t offset);
+
+/*
  * Device-side fault word of the current device: bit 0 = an mbarrier wait in a
- * kernel gave up after its iteration bound.  Reading it synchronises the
+ * kernel gave up after its time bound; bit 1 = a wait for a neighbouring
+ * GPU's halo flag gave up.  Reading it synchronises the
  * device.  pla_clear_device_faults() zeroes it.
  */
 PLA_API int pla_read_device_faults(unsigned int* faults);

@@ -40,6 +40,11 @@ SIGNATURES = {
     "pla_stencil7x7_iterate_taps": ([_vp, _f32p, _f32p, _vp, _vp, _i32, _i32, _i32, _i32, _vp], _i32),
     "pla_stencil7x7_band_step": ([_vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _vp], _i32),
     "pla_stencil7x7_band_step_taps": ([_vp, _f32p, _f32p, _vp, _i32, _i32, _i32, _i32, _i32, _vp], _i32),
+    "pla_stencil7x7_band_step_halo": ([_vp, _f32p, _f32p, _vp, _i32, _i32, _i32, _vp, _i32, _vp, _vp, _vp, _vp,
+                                       _vp, ctypes.c_uint, _vp], _i32),
+    "pla_ipc_export": ([_vp, _vp, ctypes.POINTER(ctypes.c_uint64)], _i32),
+    "pla_ipc_import": ([_vp, ctypes.c_uint64, ctypes.POINTER(ctypes.c_void_p)], _i32),
+    "pla_ipc_close": ([_vp, ctypes.c_uint64], _i32),
     "pla_read_device_faults": ([_u32p], _i32),
     "pla_clear_device_faults": ([], _i32),
 }

@@ -218,11 +218,12 @@ int launch_tile(const void* x, const void* w, const void* b, const HostTaps* ht,
   a.y_row_stride = y_row_stride;
   const long long slots = static_cast<long long>(d->sms) * per_sm;
   const int grid = static_cast<int>(total < slots ? total : slots);
+  const HaloLinks no_halo{};
   if (ht) {
-    tile_kernel<T, R, LX, true><<<grid, kTileThreads, G::SMEM, stream>>>(map, a, *ht);
+    tile_kernel<T, R, LX, true><<<grid, kTileThreads, G::SMEM, stream>>>(map, a, *ht, no_halo);
   } else {
     HostTaps unused{};
-    tile_kernel<T, R, LX, false><<<grid, kTileThreads, G::SMEM, stream>>>(map, a, unused);
+    tile_kernel<T, R, LX, false><<<grid, kTileThreads, G::SMEM, stream>>>(map, a, unused, no_halo);
   }
   PLA_CUDA(cudaGetLastError());
   return PLA_OK;
@@ -266,6 +267,84 @@ int launch_tile_dtype(int dtype, const void* x, const void* w, const void* b, co
     default:
       return PLA_ERR_UNSUPPORTED;
   }
+}
+
+// One fused band step with the halo exchange over peer memory (wide tiles,
+// host taps, one plane).  `links` carries the peer pointers and flags.
+template <typename T>
+int launch_tile_halo(const void* in, const HostTaps& ht, void* out_rows, int dtype, int rows, int width,
+                     HaloLinks links, cudaStream_t stream) {
+  using G = TileGeom<T, kWideR, kWideLX>;
+  int st;
+  DeviceInfo* d = device_info(&st);
+  if (!d) return st;
+  if (rows < 2 * G::TH) return PLA_ERR_UNSUPPORTED;  // edge tile rows must not overlap
+  CUtensorMap map;
+  const long long band = static_cast<long long>(rows + 6) * width;
+  st = make_tile_map<T, G>(&map, in, dtype, width, rows + 6, 1, width, band);
+  if (st != PLA_OK) return st;
+  int per_sm = 1;
+  st = kernel_setup<tile_kernel<T, kWideR, kWideLX, true, true>>(kTileThreads, G::SMEM, &per_sm);
+  if (st != PLA_OK) return st;
+  TileArgs a;
+  a.w = nullptr;
+  a.b = nullptr;
+  a.y = out_rows;
+  a.planes = 1;
+  a.C = 1;
+  a.W = width;
+  a.row_begin = 0;
+  a.row_end = rows;
+  a.in_row_shift = 3;
+  a.tiles_x = (width + G::TW - 1) / G::TW;
+  a.tiles_y = (rows + G::TH - 1) / G::TH;
+  const long long total = static_cast<long long>(a.tiles_x) * a.tiles_y;
+  if (total > 0x7fffffffll) return PLA_ERR_TOO_LARGE;
+  a.total_tiles = static_cast<int>(total);
+  a.div_tx = make_fastdiv(a.tiles_x);
+  a.div_ty = make_fastdiv(a.tiles_y);
+  a.div_c = make_fastdiv(1);
+  a.y_plane_stride = band;
+  a.y_row_stride = width;
+  links.rows = rows;
+  links.bot0 = (rows - 3) / G::TH;
+  links.n_top = a.tiles_x;
+  links.n_bot = a.tiles_x * (a.tiles_y - links.bot0);
+  const long long slots = static_cast<long long>(d->sms) * per_sm;
+  const int grid = static_cast<int>(total < slots ? total : slots);
+  tile_kernel<T, kWideR, kWideLX, true, true><<<grid, kTileThreads, G::SMEM, stream>>>(map, a, ht, links);
+  PLA_CUDA(cudaGetLastError());
+  return PLA_OK;
+}
+
+// ---- CUDA IPC for peer buffers ----------------------------------------------
+typedef CUresult (*PfnMemGetAddressRange)(CUdeviceptr*, size_t*, CUdeviceptr);
+PfnMemGetAddressRange g_get_range = nullptr;
+std::once_flag g_get_range_once;
+
+int alloc_base(const void* ptr, void** base) {
+  std::call_once(g_get_range_once, []() {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuMemGetAddressRange", &p, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_get_range = reinterpret_cast<PfnMemGetAddressRange>(p);
+  });
+  if (!g_get_range) {
+    std::snprintf(g_last_cuda_error, sizeof(g_last_cuda_error), "cuMemGetAddressRange unavailable");
+    return PLA_ERR_CUDA;
+  }
+  CUdeviceptr b = 0;
+  size_t size = 0;
+  CUresult r = g_get_range(&b, &size, reinterpret_cast<CUdeviceptr>(ptr));
+  if (r != CUDA_SUCCESS) {
+    std::snprintf(g_last_cuda_error, sizeof(g_last_cuda_error), "cuMemGetAddressRange failed (%d)",
+                  static_cast<int>(r));
+    return PLA_ERR_CUDA;
+  }
+  *base = reinterpret_cast<void*>(b);
+  return PLA_OK;
 }
 
 // Host taps (fp32) -> kernel-parameter filter.
@@ -670,6 +749,64 @@ int pla_stencil7x7_iterate_noalloc(const void* x, const void* w, const void* b, 
   const int st = noalloc_scratch(&scratch);
   if (st != PLA_OK) return st;
   return iterate_impl(x, w, b, nullptr, y, scratch, h, width, steps, dtype, stream);
+}
+
+int pla_stencil7x7_band_step_halo(const void* in, const float* taps, const float* bias, void* out, int rows,
+                                  int width, int dtype, void* up_out, int up_rows, void* down_out,
+                                  unsigned int* flags, unsigned int* up_flags, unsigned int* down_flags,
+                                  unsigned int* counters, unsigned int step, pla_stream_t stream) {
+  if (dtype != PLA_F32 && dtype != PLA_BF16 && dtype != PLA_F16) return PLA_ERR_UNSUPPORTED;
+  if (!in || !taps || !out || !flags || !counters || rows <= 0 || width <= 0) return PLA_ERR_INVALID_ARGUMENT;
+  if ((up_out && (!up_flags || up_rows < 3)) || (down_out && !down_flags)) return PLA_ERR_INVALID_ARGUMENT;
+  const size_t es = dtype_size(dtype);
+  const long long band = static_cast<long long>(rows + 6) * width;
+  void* out_rows = static_cast<char*>(out) + 3ll * width * es;
+  if (!tile_path_ok(in, out_rows, dtype, width, width, band, 1)) return PLA_ERR_UNSUPPORTED;
+  if ((up_out && !aligned(up_out, 16)) || (down_out && !aligned(down_out, 16))) return PLA_ERR_UNSUPPORTED;
+  const HostTaps ht = make_host_taps(taps, bias);
+  HaloLinks links{};
+  links.up_out = up_out;
+  links.down_out = down_out;
+  links.up_rows = up_rows;
+  links.flags = flags;
+  links.up_flags = up_flags;
+  links.down_flags = down_flags;
+  links.counters = counters;
+  links.step = step;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case PLA_F32: return launch_tile_halo<float>(in, ht, out_rows, dtype, rows, width, links, s);
+    case PLA_BF16: return launch_tile_halo<__nv_bfloat16>(in, ht, out_rows, dtype, rows, width, links, s);
+    default: return launch_tile_halo<__half>(in, ht, out_rows, dtype, rows, width, links, s);
+  }
+}
+
+int pla_ipc_export(const void* ptr, void* handle, uint64_t* offset) {
+  if (!ptr || !handle || !offset) return PLA_ERR_INVALID_ARGUMENT;
+  void* base = nullptr;
+  int st = alloc_base(ptr, &base);
+  if (st != PLA_OK) return st;
+  cudaIpcMemHandle_t h;
+  PLA_CUDA(cudaIpcGetMemHandle(&h, base));
+  std::memcpy(handle, &h, sizeof(h));
+  *offset = static_cast<uint64_t>(static_cast<const char*>(ptr) - static_cast<const char*>(base));
+  return PLA_OK;
+}
+
+int pla_ipc_import(const void* handle, uint64_t offset, void** ptr) {
+  if (!handle || !ptr) return PLA_ERR_INVALID_ARGUMENT;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  void* base = nullptr;
+  PLA_CUDA(cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess));
+  *ptr = static_cast<char*>(base) + offset;
+  return PLA_OK;
+}
+
+int pla_ipc_close(void* ptr, uint64_t offset) {
+  if (!ptr) return PLA_ERR_INVALID_ARGUMENT;
+  PLA_CUDA(cudaIpcCloseMemHandle(static_cast<char*>(ptr) - offset));
+  return PLA_OK;
 }
 
 int pla_read_device_faults(unsigned int* faults) {

@@ -24,7 +24,8 @@ namespace pla {
 constexpr int kTaps = 49;
 constexpr int kHalo = 3;
 
-// Device fault word (bit 0: an mbarrier wait exceeded its time bound).
+// Device fault word (bit 0: an mbarrier wait exceeded its time bound;
+// bit 1: a wait for a neighbouring GPU's halo flag timed out).
 __device__ unsigned int g_device_faults;
 
 // n / d for 0 <= n < 2^31 by one multiply-high and a shift; the divisor is
@@ -137,6 +138,47 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
       if (mbar_try_wait(bar, parity)) return true;
     if (global_timer_ns() - t0 > limit_ns) {
       atomicOr(&g_device_faults, 1u);
+      return false;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// System-scope flags between GPUs (row-band halo exchange over peer memory).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ unsigned int ld_acquire_sys(const unsigned int* p) {
+  unsigned int v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys(unsigned int* p, unsigned int v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned int atom_add_acq_rel_gpu(unsigned int* p, unsigned int v) {
+  unsigned int old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// Spins until *flag >= target (the flag only grows) for at most ~limit_ns.
+// On time-out it records bit 1 in the device fault word and returns false;
+// the caller carries on (results undefined, host sees the fault).
+__device__ __forceinline__ bool wait_flag_geq(const unsigned int* flag, unsigned int target,
+                                              uint64_t limit_ns = 2000000000ull) {
+  if (ld_acquire_sys(flag) >= target) return true;
+  const uint64_t t0 = global_timer_ns();
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 32; ++i) {
+      if (ld_acquire_sys(flag) >= target) return true;
+      __nanosleep(128);
+    }
+    if (global_timer_ns() - t0 > limit_ns) {
+      atomicOr(&g_device_faults, 2u);
       return false;
     }
   }

@@ -62,13 +62,46 @@ struct TileArgs {
   long long y_row_stride;   // elements
 };
 
+// Row-band halo exchange over peer memory (HALO kernels only).  The band of
+// this GPU is band rows [0, rows) of buffers laid out as in
+// pla_stencil7x7_band_step; its neighbours' `out` buffers are mapped here
+// (CUDA IPC).  Step s: tiles holding band rows 0..2 ("top edge") and
+// rows-3..rows-1 ("bottom edge") are visited first; before loading its input a
+// top (bottom) edge tile waits until flags[0] (flags[1]) >= s, i.e. until the
+// neighbour above (below) has delivered its step s-1 rows into this GPU's
+// halo; after storing, edge tiles also store their 3 rows into the
+// neighbour's halo rows, and the last edge tile of a side raises that
+// neighbour's flag to s+1 (release, system scope).  Counters are per side,
+// monotonic across steps (expected (s+1) x tiles of that side).
+struct HaloLinks {
+  void* up_out;             // neighbour above: its out buffer (peer memory), or nullptr
+  void* down_out;           // neighbour below: its out buffer (peer memory), or nullptr
+  int up_rows;              // band rows of the neighbour above
+  int rows;                 // band rows here
+  int bot0;                 // first tile row holding band row rows-3
+  int n_top, n_bot;         // edge tiles per side
+  unsigned int* flags;      // this GPU: [0] delivered by up, [1] delivered by down
+  unsigned int* up_flags;   // neighbour above's flags (peer memory)
+  unsigned int* down_flags; // neighbour below's flags (peer memory)
+  unsigned int* counters;   // this GPU: edge tiles finished, [0] top, [1] bottom
+  unsigned int step;
+};
+
+// Visit order of tile rows for HALO launches: the top edge row, the bottom
+// edge rows, then the rest.
+__device__ __forceinline__ int halo_tile_row(int q, int tiles_y, int bot0) {
+  if (q == 0) return 0;
+  const int nb = tiles_y - bot0;
+  return q <= nb ? bot0 + q - 1 : q - nb;
+}
+
 // HOST_TAPS: one filter for every plane, read from the HostTaps parameter;
 // otherwise plane p uses the device filter a.w[(p % C) * 49 ...] held in
 // registers.
-template <typename T, int R, int LX, bool HOST_TAPS>
+template <typename T, int R, int LX, bool HOST_TAPS, bool HALO = false>
 __global__ void __launch_bounds__(kTileThreads, HOST_TAPS ? 5 : 4)
     tile_kernel(const __grid_constant__ CUtensorMap tmap, const TileArgs a,
-                const __grid_constant__ HostTaps taps) {
+                const __grid_constant__ HostTaps taps, const __grid_constant__ HaloLinks h) {
   using G = TileGeom<T, R, LX>;
   extern __shared__ __align__(128) unsigned char smem[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 2 * G::STAGE);
@@ -94,7 +127,14 @@ __global__ void __launch_bounds__(kTileThreads, HOST_TAPS ? 5 : 4)
     const int q = fdiv(tile, a.div_tx);
     const int tx = tile - q * a.tiles_x;
     const int plane = fdiv(q, a.div_ty);
-    const int ty = q - plane * a.tiles_y;
+    int ty = q - plane * a.tiles_y;
+    if (HALO) {
+      ty = halo_tile_row(ty, a.tiles_y, h.bot0);
+      // The halo rows this tile reads arrive from the neighbours.
+      if (ty == 0 && h.up_out) wait_flag_geq(&h.flags[0], h.step);
+      if (ty >= h.bot0 && h.down_out) wait_flag_geq(&h.flags[1], h.step);
+      fence_proxy_async_global();
+    }
     const int x0 = tx * G::TW - G::LEFT;
     const int y0 = a.row_begin + ty * G::TH + a.in_row_shift - kHalo;
     fence_proxy_async_smem();
@@ -117,7 +157,8 @@ __global__ void __launch_bounds__(kTileThreads, HOST_TAPS ? 5 : 4)
     const int q = fdiv(t, a.div_tx);
     const int tx = t - q * a.tiles_x;
     const int plane = fdiv(q, a.div_ty);
-    const int ty = q - plane * a.tiles_y;
+    int ty = q - plane * a.tiles_y;
+    if (HALO) ty = halo_tile_row(ty, a.tiles_y, h.bot0);
     if (!HOST_TAPS) {
       const int c = plane - fdiv(plane, a.div_c) * a.C;
       if (c != cur_c) {
@@ -183,6 +224,37 @@ __global__ void __launch_bounds__(kTileThreads, HOST_TAPS ? 5 : 4)
 #pragma unroll
       for (int r = 0; r < R; ++r)
         if (oy0 + r < a.row_end) store4(yp + r * a.y_row_stride, acc[r][0], acc[r][1], acc[r][2], acc[r][3]);
+    }
+
+    if (HALO) {
+      const bool top = ty == 0 && h.up_out != nullptr;
+      const bool bot = ty >= h.bot0 && h.down_out != nullptr;
+      if (top || bot) {
+        if (ox < a.W) {
+#pragma unroll
+          for (int r = 0; r < R; ++r) {
+            const int oy = oy0 + r;
+            if (top && oy < 3)  // neighbour above: its bottom halo rows up_rows+3 .. up_rows+5
+              store4(static_cast<T*>(h.up_out) + static_cast<long long>(h.up_rows + 3 + oy) * a.W + ox,
+                     acc[r][0], acc[r][1], acc[r][2], acc[r][3]);
+            if (bot && oy >= h.rows - 3 && oy < h.rows)  // neighbour below: its top halo rows 0..2
+              store4(static_cast<T*>(h.down_out) + static_cast<long long>(oy - (h.rows - 3)) * a.W + ox,
+                     acc[r][0], acc[r][1], acc[r][2], acc[r][3]);
+          }
+        }
+        __syncthreads();
+        if (tid == 0) {
+          fence_acq_rel_sys();
+          if (top && atom_add_acq_rel_gpu(&h.counters[0], 1u) + 1u == (h.step + 1u) * h.n_top) {
+            fence_acq_rel_sys();
+            st_release_sys(&h.up_flags[1], h.step + 1u);
+          }
+          if (bot && atom_add_acq_rel_gpu(&h.counters[1], 1u) + 1u == (h.step + 1u) * h.n_bot) {
+            fence_acq_rel_sys();
+            st_release_sys(&h.down_flags[0], h.step + 1u);
+          }
+        }
+      }
     }
   }
 }

@@ -8,17 +8,29 @@ re-applied every step is the Jacobi scheme with a zero boundary.
   scratch plane (``pla_stencil7x7_iterate``).
 * ``BandedStencil`` — the grid split into row bands, one band per rank of a
   process group (one process per GPU).  Each band lives in two
-  (rows + 6) x W buffers whose 3 top / 3 bottom rows are halos.  A step
-  computes the 3 edge rows at each end of the band first, hands them to the
-  neighbours (NCCL send/recv on a side stream into their halo rows) and
-  computes the interior rows while the exchange is in flight.  Bands at the
-  top / bottom of the grid keep zero halos (the Dirichlet boundary).  Every
-  point is computed exactly as on one device, so the result is bit-identical
-  to ``stencil7x7_iterate`` for any number of ranks.
+  (rows + 6) x W buffers whose 3 top / 3 bottom rows are halos; bands at the
+  top / bottom of the grid keep zero halos (the Dirichlet boundary).  Two
+  exchange modes:
+
+  - ``"p2p"`` (default on GPUs): one fused kernel per step
+    (``pla_stencil7x7_band_step_halo``).  The buffers of the neighbours are
+    mapped into this process with CUDA IPC; the kernel visits the edge tiles
+    first, stores their rows straight into the neighbours' halo rows over
+    NVLink and raises a flag in the neighbour's memory; a neighbour's edge
+    tiles wait on that flag (bounded) before loading their halo.  No
+    collective call and no host round trip per step.
+  - ``"nccl"``: the 3 edge rows at each end are computed first, handed over
+    with NCCL send/recv on a side stream while the interior is computed
+    (also the path gloo CPU ranks take in the tests).
+
+  Every point is computed exactly as on one device, so the result is
+  bit-identical to ``stencil7x7_iterate`` for any number of ranks.
 """
 from __future__ import annotations
 
 from typing import Callable, Optional
+
+import ctypes
 
 import torch
 import torch.distributed as dist
@@ -101,7 +113,7 @@ class BandedStencil:
 
     def __init__(self, H: int, W: int, weight: torch.Tensor, bias: torch.Tensor | None = None,
                  group=None, device: torch.device | None = None, step_fn: StepFn | None = None,
-                 overlap: bool = True):
+                 overlap: bool = True, mode: str = "auto"):
         self.group = group
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
@@ -114,13 +126,78 @@ class BandedStencil:
         self.dtype = weight.dtype
         self.weight = weight.detach().reshape(49).contiguous()
         self.bias = None if bias is None else bias.detach().reshape(1).contiguous()
-        self.step_fn = step_fn or _cuda_band_step(self.weight, self.bias)
-        self.bufs = [torch.zeros(self.rows + 6, W, dtype=self.dtype, device=self.device) for _ in range(2)]
-        self.cur = 0
-        self.overlap = overlap and self.device.type == "cuda" and self.rows >= 12
-        self.comm_stream = torch.cuda.Stream(self.device) if self.device.type == "cuda" else None
         self.up = self.rank - 1 if self.rank > 0 else None
         self.down = self.rank + 1 if self.rank < self.world - 1 else None
+        if mode == "auto":
+            mode = "p2p" if (self.device.type == "cuda" and self.world > 1 and step_fn is None) else "nccl"
+        if mode not in ("p2p", "nccl"):
+            raise ValueError("mode must be 'p2p', 'nccl' or 'auto'")
+        if mode == "p2p" and (self.device.type != "cuda" or step_fn is not None):
+            raise ValueError("the p2p exchange runs the CUDA kernel on CUDA devices")
+        self.mode = mode
+        self.cur = 0
+        self.step_idx = 0
+        band = (self.rows + 6) * W
+        es = torch.tensor([], dtype=self.dtype).element_size()
+        if mode == "p2p":
+            # One allocation per rank so that a neighbour maps it with one IPC
+            # handle: [buffer 0 | buffer 1 | flags u32[2] | counters u32[2]].
+            self._store = torch.zeros(2 * band * es + 16, dtype=torch.uint8, device=self.device)
+            self.bufs = [self._store[k * band * es:(k + 1) * band * es].view(self.dtype).view(self.rows + 6, W)
+                         for k in range(2)]
+            self._flags = self._store[2 * band * es:2 * band * es + 8]
+            self._counters = self._store[2 * band * es + 8:2 * band * es + 16]
+            self._taps = _lib.HostTaps().update(self.weight, self.bias)
+            self._peers = {}
+            self._exchange_handles(es)
+            self._armed = False
+        else:
+            self.bufs = [torch.zeros(self.rows + 6, W, dtype=self.dtype, device=self.device) for _ in range(2)]
+        self.step_fn = step_fn or (None if mode == "p2p" else _cuda_band_step(self.weight, self.bias))
+        self.overlap = overlap and self.device.type == "cuda" and self.rows >= 12
+        self.comm_stream = torch.cuda.Stream(self.device) if self.device.type == "cuda" else None
+
+    # -- peer mapping (p2p mode) -------------------------------------------------
+    def _exchange_handles(self, es: int) -> None:
+        L = _lib.lib()
+        h = (ctypes.c_ubyte * 64)()
+        off = ctypes.c_uint64()
+        with torch.cuda.device(self.device):
+            _lib.check(L.pla_ipc_export(self._store.data_ptr(), h, ctypes.byref(off)), "pla_ipc_export")
+        info = [None] * self.world
+        dist.all_gather_object(info, (bytes(h), off.value, self.rows), group=self.group)
+        for name, peer in (("up", self.up), ("down", self.down)):
+            if peer is None:
+                continue
+            hb, poff, prows = info[peer]
+            ptr = ctypes.c_void_p()
+            with torch.cuda.device(self.device):
+                _lib.check(L.pla_ipc_import((ctypes.c_ubyte * 64).from_buffer_copy(hb), poff, ctypes.byref(ptr)),
+                           "pla_ipc_import")
+            base = ptr.value
+            pband = (prows + 6) * self.W * es
+            self._peers[name] = {"base": base, "offset": poff, "rows": prows,
+                                 "bufs": [base, base + pband], "flags": base + 2 * pband}
+
+    def close(self) -> None:
+        """Unmap the neighbours' buffers (p2p mode).  Collective: every rank calls it."""
+        if self.mode != "p2p" or not self._peers:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)  # no neighbour still writes into our halos
+        L = _lib.lib()
+        with torch.cuda.device(self.device):
+            for p in self._peers.values():
+                L.pla_ipc_close(p["base"], p["offset"])
+        self._peers = {}
+
+    def check_faults(self) -> None:
+        """Raise if a kernel on this device gave up a bounded wait (synchronises)."""
+        v = ctypes.c_uint(0)
+        with torch.cuda.device(self.device):
+            _lib.check(_lib.lib().pla_read_device_faults(ctypes.byref(v)), "pla_read_device_faults")
+        if v.value:
+            raise _lib.PlaError(f"device fault word {v.value:#x}: a bounded wait in a kernel timed out")
 
     def _global(self, peer: int) -> int:
         return peer if self.group is None else dist.get_global_rank(self.group, peer)
@@ -133,6 +210,8 @@ class BandedStencil:
         a0, a1 = max(0, self.r0 - 3), min(self.H, self.r1 + 3)
         b[3 - (self.r0 - a0):3 + self.rows + (a1 - self.r1)].copy_(grid[a0:a1])
         self.bufs[1 - self.cur].zero_()
+        if self.mode == "p2p":
+            self._armed = False  # neighbours must finish loading before anyone steps
 
     def band(self) -> torch.Tensor:
         """This rank's current band rows [rows, W] (a view)."""
@@ -170,7 +249,30 @@ class BandedStencil:
             ops.append(dist.P2POp(dist.irecv, dst[R + 3:R + 6], self._global(self.down), self.group))
         return ops
 
+    def _step_p2p(self) -> None:
+        if not self._armed:
+            torch.cuda.synchronize(self.device)
+            dist.barrier(group=self.group)
+            self._armed = True
+        L = _lib.lib()
+        nxt = 1 - self.cur
+        up, down = self._peers.get("up"), self._peers.get("down")
+        taps, hb = self._taps.args()
+        flags = self._flags.data_ptr()
+        st = L.pla_stencil7x7_band_step_halo(
+            self.bufs[self.cur].data_ptr(), taps, hb, self.bufs[nxt].data_ptr(), self.rows, self.W,
+            _lib.DTYPE_CODE[self.dtype],
+            up["bufs"][nxt] if up else None, up["rows"] if up else 0,
+            down["bufs"][nxt] if down else None,
+            flags, up["flags"] if up else None, down["flags"] if down else None,
+            self._counters.data_ptr(), self.step_idx, _lib.stream_ptr(self.device))
+        _lib.check(st, "pla_stencil7x7_band_step_halo")
+        self.step_idx += 1
+        self.cur = nxt
+
     def step(self) -> None:
+        if self.mode == "p2p":
+            return self._step_p2p()
         src, dst = self.bufs[self.cur], self.bufs[1 - self.cur]
         R = self.rows
         if self.overlap and self.world > 1:

@@ -1,5 +1,6 @@
-"""Multi-GPU parity: the row-band iterated stencil over NCCL (one process per
-GPU) must equal the single-GPU iteration bit for bit.  Needs >= 2 GPUs."""
+"""Multi-GPU parity: the row-band iterated stencil (one process per GPU; halo
+exchange fused into the kernel over peer memory, or over NCCL) must equal the
+single-GPU iteration bit for bit.  Needs >= 2 GPUs; ranks never share a GPU."""
 import os
 import random
 import socket
@@ -24,7 +25,7 @@ def _inputs(H, W):
     return x, w / w.sum()
 
 
-def _rank(rank, world, port, H, W, steps, q):
+def _rank(rank, world, port, H, W, steps, mode, q):
     import datetime
 
     import torch.distributed as dist
@@ -38,21 +39,25 @@ def _rank(rank, world, port, H, W, steps, q):
         from pla_b200 import BandedStencil
 
         x, w = _inputs(H, W)
-        bs = BandedStencil(H, W, w.to(dev), device=dev)
+        bs = BandedStencil(H, W, w.to(dev), device=dev, mode=mode)
+        assert bs.mode == mode
         bs.load(x.to(dev))
         bs.run(steps)
         full = bs.gather()
         torch.cuda.synchronize()
+        bs.check_faults()
         if rank == 0:
             q.put(full.cpu())
+        bs.close()
         dist.barrier()
     finally:
         dist.destroy_process_group()
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("world,H,W,steps", [(2, 1000, 768, 9), (2, 64, 256, 5)])
-def test_banded_nccl_equals_single_gpu(world, H, W, steps):
+@pytest.mark.parametrize("mode", ["p2p", "nccl"])
+@pytest.mark.parametrize("world,H,W,steps", [(2, 1000, 768, 9), (2, 300, 256, 12)])
+def test_banded_multi_gpu_equals_single_gpu(world, H, W, steps, mode):
     from pla_b200 import stencil7x7_iterate
 
     x, w = _inputs(H, W)
@@ -60,7 +65,7 @@ def test_banded_nccl_equals_single_gpu(world, H, W, steps):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank, args=(r, world, port, H, W, steps, q)) for r in range(world)]
+    procs = [ctx.Process(target=_rank, args=(r, world, port, H, W, steps, mode, q)) for r in range(world)]
     for p in procs:
         p.start()
     got = q.get(timeout=180)
