@@ -17,7 +17,14 @@ from __future__ import annotations
 
 import torch
 
-from . import _lib
+if __package__:
+    from . import _lib
+else:  # loaded from its path by a KernelBench-style harness (run_and_check)
+    import os
+    import sys
+
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    from pla_b200 import _lib
 
 
 def depthwise7x7(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None,

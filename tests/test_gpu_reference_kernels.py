@@ -1,0 +1,135 @@
+"""Head-to-head with the reference's own stencil CUDA kernels on the B200.
+
+oracle/Makefile (`make -C oracle ref REF=<PLA checkout>`, run by
+__graft_entry__.build() when the reference tree is next to this repository)
+compiles, unmodified and for sm_100a, the kernels behind
+``launch_direct`` (data/stencil_direct_cuda_v7/stencil_cuda_kernel.cu:230-244)
+and ``launch_stencil`` (data/stencil_cuda_v2/stencil_cuda_kernel.cu:195-209)
+into oracle/_ref/.  These tests check this library against them on the
+reference harness shape (data/stencil_7x7.py:17-20, 1x1x10240x10240) and on
+cfg2's 4096^2, and print both kernels' times (``pytest -s`` shows them).
+
+v7 accumulates in fp32 in (row, column) tap order and adds the bias before
+the cast (stencil_cuda_kernel.cu:64-71) — the same arithmetic as this
+library — so it must agree bit for bit; v2 uses mma.sync tiles (another
+summation order) and rounds to fp16 before adding the bias
+(stencil_cuda_kernel.cu:103-106), so it is compared within fp16 tolerance.
+"""
+import ctypes
+import os
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+REF = os.path.join(ROOT, "oracle", "_ref")
+V7 = os.path.join(REF, "libref_stencil_v7.so")
+V2 = os.path.join(REF, "libref_stencil_v2.so")
+_vp, _i, _i64 = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64
+
+
+def _v7():
+    lib = ctypes.CDLL(V7)
+    f = lib["_Z13launch_directPKvS0_S0_PviiillliP11CUstream_st"]
+    f.argtypes = [_vp, _vp, _vp, _vp, _i, _i, _i, _i64, _i64, _i64, _i, _vp]
+    f.restype = None
+    return f
+
+
+def _v2():
+    lib = ctypes.CDLL(V2)
+    f = lib["_Z14launch_stencilPKvS0_S0_PviiibP11CUstream_st"]
+    f.argtypes = [_vp, _vp, _vp, _vp, _i, _i, _i, ctypes.c_bool, _vp]
+    f.restype = None
+    return f
+
+
+def _time(fn, iters=20, warmup=3):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(iters):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / iters
+
+
+def _inputs(H, W, dtype):
+    g = torch.Generator().manual_seed(1)
+    x = (torch.rand(1, 1, H, W, generator=g) * 2 - 1).to(dtype).cuda()
+    w = ((torch.rand(1, 1, 7, 7, generator=g) * 2 - 1) / 49).to(dtype).cuda()
+    b = ((torch.rand(1, generator=g) * 2 - 1) / 49).to(dtype).cuda()
+    return x, w, b
+
+
+@pytest.mark.skipif(not os.path.exists(V7), reason="reference kernels not built (oracle/_ref)")
+@pytest.mark.parametrize("H,W", [(10240, 10240), (4096, 4096)])
+@pytest.mark.parametrize("dtype", [torch.float16, torch.float32])
+def test_against_reference_v7(H, W, dtype):
+    from pla_b200.stencil import ModelNew
+
+    x, w, b = _inputs(H, W, dtype)
+    code = {torch.float16: 0, torch.float32: 1}[dtype]
+    launch = _v7()
+    y_ref = torch.empty_like(x)
+    stream = torch.cuda.current_stream().cuda_stream
+
+    def ref():
+        launch(x.data_ptr(), w.data_ptr(), b.data_ptr(), y_ref.data_ptr(), 1, H, W, H * W, W, 1, code, stream)
+
+    m = ModelNew().cuda().to(dtype)
+    with torch.no_grad():
+        m.conv1.weight.copy_(w)
+        m.conv1.bias.copy_(b)
+    y = torch.empty_like(x)
+
+    def ours():
+        m(x, out=y)
+
+    ref()
+    ours()
+    torch.cuda.synchronize()
+    assert torch.equal(y, y_ref)
+    t_ref, t_ours = _time(ref), _time(ours)
+    pts = H * W
+    print(f"\n[v7 {str(dtype)[6:]} {H}x{W}] reference launch_direct {t_ref * 1e3:.1f} us "
+          f"({pts / t_ref / 1e6:.0f} GPt/s), pla_b200 {t_ours * 1e3:.1f} us ({pts / t_ours / 1e6:.0f} GPt/s), "
+          f"speed-up {t_ref / t_ours:.2f}x")
+
+
+@pytest.mark.skipif(not os.path.exists(V2), reason="reference kernels not built (oracle/_ref)")
+@pytest.mark.parametrize("H,W", [(10240, 10240), (4096, 4096)])
+def test_against_reference_v2_fp16(H, W):
+    from pla_b200.stencil import ModelNew
+
+    x, w, b = _inputs(H, W, torch.float16)
+    launch = _v2()
+    y_ref = torch.empty_like(x)
+    stream = torch.cuda.current_stream().cuda_stream
+
+    def ref():
+        launch(x.data_ptr(), w.data_ptr(), b.data_ptr(), y_ref.data_ptr(), 1, H, W, True, stream)
+
+    m = ModelNew().cuda().half()
+    with torch.no_grad():
+        m.conv1.weight.copy_(w)
+        m.conv1.bias.copy_(b)
+    y = torch.empty_like(x)
+
+    def ours():
+        m(x, out=y)
+
+    ref()
+    ours()
+    torch.cuda.synchronize()
+    torch.testing.assert_close(y.float(), y_ref.float(), atol=2e-3, rtol=2e-3)
+    t_ref, t_ours = _time(ref), _time(ours)
+    pts = H * W
+    print(f"\n[v2 fp16 {H}x{W}] reference launch_stencil (mma.sync) {t_ref * 1e3:.1f} us "
+          f"({pts / t_ref / 1e6:.0f} GPt/s), pla_b200 {t_ours * 1e3:.1f} us ({pts / t_ours / 1e6:.0f} GPt/s), "
+          f"speed-up {t_ref / t_ours:.2f}x")
