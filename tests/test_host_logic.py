@@ -104,3 +104,42 @@ def test_banded_iterate_gloo_matches_single_domain(world, H, W, steps):
     w = w / w.sum()
     ref = oracle.stencil7x7_iterate(x, w, steps)
     assert torch.equal(full, ref)
+
+
+# ---- a rank that leaves: the others get an error, not a hang -------------------
+def _leaver_main(rank, world, port, out_q):
+    import datetime
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+    from pla_b200.iterate import BandedStencil
+
+    g = torch.Generator().manual_seed(4)
+    x = torch.rand(24, 16, generator=g)
+    w = torch.rand(7, 7, generator=g)
+    bs = BandedStencil(24, 16, w, device=torch.device("cpu"), step_fn=_oracle_band_step(w))
+    bs.load(x)
+    if rank == 1:
+        os._exit(0)  # leaves between steps, before any exchange
+    try:
+        bs.run(3)
+        out_q.put("no error")
+    except Exception as exc:  # noqa: BLE001
+        out_q.put(type(exc).__name__)
+    out_q.close()
+    out_q.join_thread()  # flush the queue's feeder thread before the hard exit
+    os._exit(0)
+
+
+def test_rank_leaving_raises_on_the_survivor():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29500 + random.Random(77).randrange(5000, 9000)
+    procs = [ctx.Process(target=_leaver_main, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    outcome = q.get(timeout=120)
+    for p in procs:
+        p.join(timeout=60)
+    assert outcome != "no error"
