@@ -133,3 +133,77 @@ def test_against_reference_v2_fp16(H, W):
     print(f"\n[v2 fp16 {H}x{W}] reference launch_stencil (mma.sync) {t_ref * 1e3:.1f} us "
           f"({pts / t_ref / 1e6:.0f} GPt/s), pla_b200 {t_ours * 1e3:.1f} us ({pts / t_ours / 1e6:.0f} GPt/s), "
           f"speed-up {t_ref / t_ours:.2f}x")
+
+
+# ---------------------------------------------------------------------------
+# the reference's CUTLASS depthwise kernels (K1-K6 of the survey):
+# data/depthwise_conv_7x7_cuda/model_cutlass.py (v1), model_cutlass_autotune_v5.py,
+# model_cutlass_autotune_v6.py, launch_depthwise_7x7_cutlass(x, packed_w, y,
+# n, c, h, w, fp16, stream); CUDA source strings compiled unmodified for
+# sm_100a against CUTLASS headers (oracle/Makefile, target `ref`).
+# ---------------------------------------------------------------------------
+def _dw(tag):
+    lib = ctypes.CDLL(os.path.join(REF, f"libref_dw_{tag}.so"))
+    f = lib["_Z28launch_depthwise_7x7_cutlassPKvS0_PviiiibP11CUstream_st"]
+    f.argtypes = [_vp, _vp, _vp, _i, _i, _i, _i, ctypes.c_bool, _vp]
+    f.restype = None
+    return f
+
+
+def _pack_weight(w: torch.Tensor) -> torch.Tensor:
+    """The reference's [C,1,7,7] -> [C,8,80] packing (model_cutlass_autotune_v6.py:484-492,
+    identical in model_cutlass.py:305-313 and model_cutlass_autotune_v5.py:445-453):
+    row m = 2x4 output position (m // 2, m % 2), column k = input offset (k // 8, k % 8)."""
+    m = torch.arange(8, device=w.device)[:, None]
+    k = torch.arange(80, device=w.device)[None, :]
+    ky = k // 8 - m // 2
+    kx = k % 8 - m % 2
+    valid = (ky >= 0) & (ky < 7) & (kx >= 0) & (kx < 7)
+    vals = w[:, 0, ky.clamp(0, 6), kx.clamp(0, 6)]
+    return torch.where(valid[None], vals, torch.zeros_like(vals)).contiguous()
+
+
+@pytest.mark.skipif(not os.path.exists(os.path.join(REF, "libref_dw_v6.so")),
+                    reason="reference CUTLASS depthwise kernels not built (oracle/_ref)")
+@pytest.mark.parametrize("shape", [(1, 8, 2048, 2048), (1, 32, 1024, 1024)])
+@pytest.mark.parametrize("dtype", [torch.float16, torch.float32])
+def test_against_reference_cutlass_depthwise(shape, dtype):
+    from pla_b200.depthwise import ModelNew
+
+    N, C, H, W = shape
+    g = torch.Generator().manual_seed(2)
+    x = torch.rand(shape, generator=g).to(dtype).cuda()               # harness draw: torch.rand
+    w = ((torch.rand(C, 1, 7, 7, generator=g) * 2 - 1) / 7).to(dtype).cuda()  # Conv2d default-init range
+    packed = _pack_weight(w)
+    stream = torch.cuda.current_stream().cuda_stream
+    m = ModelNew(C, 7, 1, 3).cuda().to(dtype)
+    with torch.no_grad():
+        m.conv2d.weight.copy_(w)
+    y = torch.empty_like(x)
+
+    from pla_b200.depthwise import depthwise7x7
+
+    def ours():
+        depthwise7x7(x, m.conv2d.weight, None, out=y)
+
+    ours()
+    want = torch.nn.functional.conv2d(x.float().cpu(), w.float().cpu(), padding=3, groups=C)
+    # 1e-2 for low precision, as the reference's own checks (benchmark/MetaSchedule/common.py:181-191)
+    tol = 1e-2 if dtype == torch.float16 else 1e-5
+    torch.testing.assert_close(y.float().cpu(), want.to(dtype).float(), atol=tol, rtol=tol)
+    pts = N * C * H * W
+    t_ours = _time(ours)
+    line = f"\n[depthwise {str(dtype)[6:]} {N}x{C}x{H}x{W}] pla_b200 {t_ours * 1e3:.1f} us ({pts / t_ours / 1e6:.0f} GPt/s)"
+    for tag in ("v1", "v5", "v6"):
+        launch = _dw(tag)
+        y_ref = torch.empty_like(x)
+
+        def ref():
+            launch(x.data_ptr(), packed.data_ptr(), y_ref.data_ptr(), N, C, H, W, dtype == torch.float16, stream)
+
+        ref()
+        torch.cuda.synchronize()
+        torch.testing.assert_close(y_ref.float().cpu(), want.to(dtype).float(), atol=tol, rtol=tol)
+        t_ref = _time(ref)
+        line += f"; ref {tag} {t_ref * 1e3:.1f} us ({t_ref / t_ours:.2f}x)"
+    print(line)
