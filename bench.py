@@ -6,7 +6,7 @@ depthwise hot path on 1..8 B200s, with the reference's CPU path beside it.
                     [--workload NAME]
 
 N > 1 is launched one process per GPU by torch.distributed.run.  Rank 0 prints
-one JSON line.  Workloads (BASELINE configurations; synthetic seeded inputs):
+one JSON line.  Workloads (the benchmark configurations; synthetic seeded inputs):
 
   stencil_cfg2   (default) single-step 7x7 stencil, fp32 1x1x4096x4096, seed 1;
                  one grid per GPU (weak scaling, no collective)
@@ -705,7 +705,7 @@ def main():
             "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": K,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
             "scaling": wl.scaling, "vs_baseline": None, "dtype": wl.dtype,
-            "data": "synthetic (seeded, BASELINE recipe)", "config": wl.config(),
+            "data": "synthetic (seeded generator draws of the benchmark recipe)", "config": wl.config(),
             "gpoints_per_s": gpoints, "frac_of_8tbs": value / world / NOMINAL_HBM_GBS,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"
@@ -737,7 +737,7 @@ def run_reference(args, Wl, rank, world):
     line = {
         "metric": METRIC, "value": gbs, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": s_per * 1e3, "higher_is_better": True, "scaling": wl.scaling,
-        "vs_baseline": None, "dtype": wl.dtype, "data": "synthetic (seeded, BASELINE recipe)",
+        "vs_baseline": None, "dtype": wl.dtype, "data": "synthetic (seeded generator draws of the benchmark recipe)",
         "config": wl.config(), "impl": "reference", "cpu_baseline": cpu,
         "e2e": {"value": gbs, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }

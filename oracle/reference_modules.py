@@ -1,4 +1,4 @@
-"""The reference's two problem modules, re-declared — TEST/BASELINE INFRASTRUCTURE ONLY.
+"""The reference's two problem modules, re-declared — TEST AND CPU-BASELINE INFRASTRUCTURE ONLY.
 
 The reference computes its hot path on the CPU with PyTorch's own
 torch.nn.Conv2d; its problem files are thin wrappers:

@@ -7,7 +7,7 @@ Run in a checkout that has the reference tree (PLA) next to it:
 It imports the reference's own ``data/stencil_7x7.py`` and
 ``data/depthwise_conv_7x7.py`` (their ``Model`` classes are plain
 torch.nn.Conv2d wrappers), loads seeded parameters into them and records their
-CPU outputs for seeded inputs.  Inputs follow BASELINE's recipes (x, w, b drawn
+CPU outputs for seeded inputs.  Inputs follow the benchmark configurations' recipes (x, w, b drawn
 in that order from ``torch.Generator().manual_seed(seed)`` on the CPU) at
 reduced sizes, plus the odd/tail shapes of the reference's own tests
 (data/stencil_direct_cuda_v7/test_stencil.py:31-37).
@@ -165,7 +165,7 @@ def main(argv=None):
     dw_case("dw_f16_14", (1, 4, 14, 14), 11, "f16")
     dw_case("dw_f32_nhwc_odd", (2, 35, 9, 10), 12, "f32", "nhwc")
 
-    # ---------------- iterated stencil (BASELINE cfg5 recipe, reduced) --------
+    # ---------------- iterated stencil (iterated-stencil recipe, reduced) --------
     g = torch.Generator().manual_seed(4)
     H = W = 64
     x = torch.rand(H, W, generator=g) * 2 - 1

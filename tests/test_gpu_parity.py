@@ -129,7 +129,7 @@ def test_updated_weights_side_stream_and_empty():
 
 
 # --------------------------------------------------------------------------
-# BASELINE configurations at full size, bit-exact against the oracle
+# benchmark configurations at full size, bit-exact against the oracle
 # --------------------------------------------------------------------------
 def _dw_inputs(seed, shape, dtype, bias=True):
     g = torch.Generator().manual_seed(seed)
