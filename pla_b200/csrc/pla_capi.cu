@@ -165,6 +165,9 @@ int make_tile_map(CUtensorMap* map, const void* x, int dtype, int width, int row
 // 33..64-wide planes (one 56 x 64 tile per ConvNeXt stage-1 plane).
 constexpr int kWideR = 8, kWideLX = 32;
 constexpr int kNarrowR = 7, kNarrowLX = 16;
+// Short narrow tiles (16 x 64) for stacks too small to give every SM a
+// 56-row tile.
+constexpr int kShortR = 2;
 
 // Can the plane-tile kernel read this stack with TMA?
 bool tile_path_ok(const void* x, const void* y, int dtype, int width, long long row_stride,
@@ -230,14 +233,18 @@ int launch_tile(const void* x, const void* w, const void* b, const HostTaps* ht,
 }
 
 template <typename T>
-int launch_tile_shape(bool narrow, const void* x, const void* w, const void* b, const HostTaps* ht, void* y,
+int launch_tile_shape(int shape, const void* x, const void* w, const void* b, const HostTaps* ht, void* y,
                       int dtype, int planes, int C, int in_rows, int width, long long x_row_stride,
                       long long x_plane_stride, int row_begin, int row_end, int in_row_shift,
                       long long y_plane_stride, long long y_row_stride, cudaStream_t stream) {
-  if (narrow)
+  if (shape == 1)
     return launch_tile<T, kNarrowR, kNarrowLX>(x, w, b, ht, y, dtype, planes, C, in_rows, width, x_row_stride,
                                                x_plane_stride, row_begin, row_end, in_row_shift, y_plane_stride,
                                                y_row_stride, stream);
+  if (shape == 2)
+    return launch_tile<T, kShortR, kNarrowLX>(x, w, b, ht, y, dtype, planes, C, in_rows, width, x_row_stride,
+                                              x_plane_stride, row_begin, row_end, in_row_shift, y_plane_stride,
+                                              y_row_stride, stream);
   return launch_tile<T, kWideR, kWideLX>(x, w, b, ht, y, dtype, planes, C, in_rows, width, x_row_stride,
                                          x_plane_stride, row_begin, row_end, in_row_shift, y_plane_stride,
                                          y_row_stride, stream);
@@ -250,7 +257,16 @@ int launch_tile_dtype(int dtype, const void* x, const void* w, const void* b, co
                       int planes, int C, int in_rows, int width, long long x_row_stride, long long x_plane_stride,
                       int row_begin, int row_end, int in_row_shift, long long y_plane_stride,
                       long long y_row_stride, cudaStream_t stream) {
-  const bool narrow = use_narrow_tiles(width, row_end - row_begin);
+  // 0: 32 x 128 tiles; 1: 56 x 64 tiles; 2: 16 x 64 tiles when 56-row tiles
+  // would leave SMs idle.
+  int narrow = use_narrow_tiles(width, row_end - row_begin) ? 1 : 0;
+  if (narrow) {
+    int st;
+    DeviceInfo* d = device_info(&st);
+    if (!d) return st;
+    const long long tall = static_cast<long long>(planes) * ((row_end - row_begin + 55) / 56);
+    if (tall < 2ll * d->sms) narrow = 2;
+  }
   switch (dtype) {
     case PLA_F32:
       return launch_tile_shape<float>(narrow, x, w, b, ht, y, dtype, planes, C, in_rows, width, x_row_stride,
