@@ -54,6 +54,16 @@ TAPS = 49
 # ---------------------------------------------------------------------------
 # helpers
 # ---------------------------------------------------------------------------
+def profiled_traffic(workload: str):
+    """DRAM bytes of one launch of the workload's dominant kernel, from profiles/traffic.json (ncu)."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
+            d = json.load(f)[workload]
+        return d["dram_read_bytes"] + d["dram_write_bytes"], d["source"]
+    except Exception:
+        return None, None
+
+
 def measured_peaks():
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
@@ -696,6 +706,7 @@ def main():
     sm_mhz = clocks.get("sm_mhz") or 1965
     fma_gpts = torch.cuda.get_device_properties(dev).multi_processor_count * FMA_PER_SM_PER_CLK * sm_mhz * 1e6 / TAPS / 1e9
 
+    traffic, traffic_src = profiled_traffic(wl.name)
     cpu_baseline = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         _, cpu_baseline = time_cpu_reference(wl, args.cpu_budget)
@@ -710,7 +721,9 @@ def main():
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"
                          if peak_kind == "measured" else "fallback 6.65 TB/s",
-                         "traffic": None, "per_launch_ms": mean_step_ms / max(1, wl.launches_per_step),
+                         "traffic": traffic, "traffic_source": traffic_src,
+                         "algorithmic_bytes_per_launch": wl.bytes // max(1, wl.launches_per_step),
+                         "per_launch_ms": mean_step_ms / max(1, wl.launches_per_step),
                          "fma_ceiling_gpoints_per_s": fma_gpts,
                          "fma_frac": (job_points / world) / (mean_step_ms * 1e-3) / 1e9 / fma_gpts},
             "cpu_baseline": cpu_baseline, "e2e": e2e,

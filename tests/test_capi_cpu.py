@@ -79,3 +79,32 @@ def test_module_interfaces_match_reference():
         depthwise.ModelNew(8, 3, 1, 1)
     with pytest.raises(ValueError):
         depthwise.ModelNew(8, 7, 1, 1)  # the reference default padding=1 is not a 7x7 "same" conv
+
+
+def test_halo_and_ipc_argument_validation_needs_no_device():
+    from pla_b200 import _lib
+
+    L = _lib.lib()
+    taps = (ctypes.c_float * 49)()
+    # bad dtype, missing buffers, neighbour without its flag word
+    assert L.pla_stencil7x7_band_step_halo(None, taps, None, None, 64, 128, 2, None, 0, None, None, None, None,
+                                           None, 0, None) == 2
+    assert L.pla_stencil7x7_band_step_halo(None, taps, None, None, 64, 128, 1, None, 0, None, None, None, None,
+                                           None, 0, None) == 1
+    assert L.pla_ipc_export(None, None, None) == 1
+    assert L.pla_ipc_import(None, 0, None) == 1
+    assert L.pla_ipc_close(None, 0) == 1
+    # the allocation-free iterate rejects grids beyond its static scratch before touching a device
+    assert L.pla_stencil7x7_iterate_noalloc(None, None, None, None, 4096, 4096, 1, 1, None) == 3
+    assert b"16777216" in L.pla_last_cuda_error()
+
+
+def test_bench_reads_profiled_traffic():
+    import importlib.util
+
+    spec = importlib.util.spec_from_file_location("bench_mod", os.path.join(ROOT, "bench.py"))
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    t, src = bench.profiled_traffic("stencil7x7_cfg2_4096x4096_f32")
+    assert t and t > 60e6 and src.endswith(".md")
+    assert bench.profiled_traffic("no-such-workload") == (None, None)
