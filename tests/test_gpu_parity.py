@@ -310,3 +310,37 @@ def test_no_device_faults_recorded():
     v = ctypes.c_uint(123)
     assert _lib.lib().pla_read_device_faults(ctypes.byref(v)) == 0
     assert v.value == 0
+
+
+def test_modules_replay_in_cuda_graph():
+    """After a warm-up call the launches are capturable: replaying a CUDA graph
+    of the modules on new inputs gives the oracle's results."""
+    from pla_b200.depthwise import ModelNew as DW
+    from pla_b200.stencil import ModelNew as ST
+
+    g = torch.Generator().manual_seed(21)
+    st_m = ST().to(DEV)
+    dw_m = DW(64, 7, 1, 3, bias=True).to(DEV).bfloat16()
+    xs = torch.rand(1, 1, 128, 256, device=DEV)
+    xd = torch.rand(4, 64, 14, 14, device=DEV).bfloat16()
+    out_s = torch.empty_like(xs)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):  # warm-up: filter caches, kernel attributes
+        st_m(xs, out=out_s)
+        dw_m(xd)
+    torch.cuda.current_stream().wait_stream(s)
+    graph = torch.cuda.CUDAGraph()
+    with torch.no_grad(), torch.cuda.graph(graph):
+        st_m(xs, out=out_s)
+        out_d = dw_m(xd)
+    new_s = torch.rand(1, 1, 128, 256, generator=g)
+    new_d = torch.rand(4, 64, 14, 14, generator=g).bfloat16()
+    xs.copy_(new_s)
+    xd.copy_(new_d)
+    graph.replay()
+    torch.cuda.synchronize()
+    w, b = st_m.conv1.weight.detach().cpu(), st_m.conv1.bias.detach().cpu()
+    _assert_equal(out_s, oracle.stencil7x7(new_s, w, b))
+    _assert_equal(out_d, oracle.depthwise7x7(new_d, dw_m.conv2d.weight.detach().cpu(),
+                                              dw_m.conv2d.bias.detach().cpu()))
