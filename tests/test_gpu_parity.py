@@ -344,3 +344,32 @@ def test_modules_replay_in_cuda_graph():
     _assert_equal(out_s, oracle.stencil7x7(new_s, w, b))
     _assert_equal(out_d, oracle.depthwise7x7(new_d, dw_m.conv2d.weight.detach().cpu(),
                                               dw_m.conv2d.bias.detach().cpu()))
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("shape,layout", [((2, 64, 14, 14), "nchw"), ((2, 64, 14, 14), "nhwc"),
+                                          ((1, 4, 56, 56), "nchw"), ((1, 2, 40, 256), "nchw")])
+def test_misaligned_inputs_take_the_fallbacks(dtype, shape, layout):
+    """Inputs whose storage starts one element past a 16-byte boundary cannot be
+    read by TMA / bulk copies; the dispatcher must route them elsewhere."""
+    from pla_b200 import depthwise7x7, stencil7x7
+
+    x, w, b = _dw_inputs(13, shape, dtype, True)
+    if layout == "nhwc":
+        x = x.contiguous(memory_format=torch.channels_last)
+    flat = torch.empty(x.numel() + 1, dtype=dtype, device=DEV)
+    if layout == "nhwc":
+        N, C, H, W = shape
+        xd = flat[1:].view(N, H, W, C).permute(0, 3, 1, 2)
+        xd.copy_(x.to(DEV))
+        assert xd.is_contiguous(memory_format=torch.channels_last)
+    else:
+        xd = flat[1:].view(shape)
+        xd.copy_(x.to(DEV))
+    assert xd.data_ptr() % 16 != 0
+    y = depthwise7x7(xd, w.to(DEV), b.to(DEV))
+    _assert_equal(y, oracle.depthwise7x7(x, w, b))
+    if shape[1] == 2:  # also as a stencil batch (2 planes of one channel each)
+        xs = xd[:, :1]
+        ys = stencil7x7(xs, w[0:1].to(DEV), b[0:1].to(DEV))
+        _assert_equal(ys, oracle.stencil7x7(x[:, :1].contiguous(), w[0:1], b[0:1]))
