@@ -463,7 +463,7 @@ int make_nhwc_map(CUtensorMap* map, const void* base, int dtype, int n, int c, i
 template <typename T, bool NHWC, int S>
 int launch_stack(const void* x, const void* w, const void* b, void* y, int dtype, int n, int c,
                  cudaStream_t stream) {
-  using G = StackGeom<S>;
+  using G = StackGeom<S, kMixStack<T>>;
   using M = StackSmem<T, S>;
   int st;
   DeviceInfo* d = device_info(&st);

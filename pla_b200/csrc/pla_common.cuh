@@ -80,6 +80,37 @@ template <> __device__ __forceinline__ double from_acc<double>(double v) { retur
 __device__ __forceinline__ float fma_rn(float a, float b, float c) { return __fmaf_rn(a, b, c); }
 __device__ __forceinline__ double fma_rn(double a, double b, double c) { return __fma_rn(a, b, c); }
 
+// Mixed-precision FMA of sm_100 (PTX fma.rn.f32.bf16 / fma.rn.f32.f16):
+// 16-bit a and b, fp32 c, a * b + c rounded once to fp32.  Widening a 16-bit
+// value to fp32 is exact, so this equals fmaf(float(a), float(b), c) bit for
+// bit (checked on B200 over 2^24 random operand triples, specials included);
+// it lets 16-bit kernels use x and w straight from packed 16-bit storage.
+// The tag argument selects the format.
+__device__ __forceinline__ float fma_mix(__nv_bfloat16, unsigned short a, unsigned short b, float c) {
+  float d;
+  asm("fma.rn.f32.bf16 %0, %1, %2, %3;" : "=f"(d) : "h"(a), "h"(b), "f"(c));
+  return d;
+}
+__device__ __forceinline__ float fma_mix(__half, unsigned short a, unsigned short b, float c) {
+  float d;
+  asm("fma.rn.f32.f16 %0, %1, %2, %3;" : "=f"(d) : "h"(a), "h"(b), "f"(c));
+  return d;
+}
+// Half `hi` (0: bits 0-15, 1: bits 16-31) of a packed pair.
+__device__ __forceinline__ unsigned short half_of(uint32_t w, int hi) {
+  unsigned short l, h;
+  asm("mov.b32 {%0, %1}, %2;" : "=h"(l), "=h"(h) : "r"(w));
+  return hi ? h : l;
+}
+// The 49 taps of filter c as packed 16-bit pairs: tap k in half k & 1 of p[k / 2].
+template <typename T>
+__device__ __forceinline__ void load_taps16(const T* w, int c, uint32_t (&p)[(kTaps + 1) / 2]) {
+  const unsigned short* wb = reinterpret_cast<const unsigned short*>(w) + c * kTaps;
+#pragma unroll
+  for (int k = 0; k < (kTaps + 1) / 2; ++k)
+    p[k] = static_cast<uint32_t>(wb[2 * k]) | (2 * k + 1 < kTaps ? static_cast<uint32_t>(wb[2 * k + 1]) << 16 : 0u);
+}
+
 // ---------------------------------------------------------------------------
 // mbarrier + TMA (cp.async.bulk.tensor) wrappers.  Loads only, never
 // multicast: every tensor map in this library covers this GPU's own memory.

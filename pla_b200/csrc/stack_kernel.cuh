@@ -10,10 +10,16 @@
 //    NHWC stages are one 4-D TMA box (LANES channels x S x S x 1 image).  Both
 //    land raw in a 2-deep shared-memory ring guarded by mbarriers, issued one
 //    stage ahead by thread 0 of a persistent CTA.
-//  * Expand: the raw stage is widened to fp32 into an "x-quad" layout
+//  * fp32 stacks: the raw stage is first copied into an "x-quad" layout
 //    F[y][x/4][lane][x%4], so that one 128-bit shared load gives a thread 4
 //    consecutive columns of its own plane and a warp's load is 512 contiguous
 //    bytes (bank-conflict free).
+//  * 16-bit stacks skip that copy: each thread reads its plane's rows straight
+//    from the raw stage (32-bit words of two columns for even-width NCHW
+//    planes, 16-bit elements otherwise) into mixed-precision FMAs (16-bit x
+//    and w, fp32 accumulator, identical bits), with the taps packed two per
+//    register.  Half the registers and no second shared buffer give 3 CTAs
+//    per SM instead of 2 at S = 14.
 //  * Compute: a thread computes R output rows x S columns of its plane with
 //    the 49 taps of its channel in registers.  Rows and columns that fall on
 //    the zero padding are skipped (compile-time for columns, a warp-uniform
@@ -29,7 +35,7 @@
 
 namespace pla {
 
-template <int S>
+template <int S, bool MIX>
 struct StackGeom {
   static_assert(S == 7 || S == 14 || S == 28, "plane side");
   static constexpr int R = (S == 7) ? 7 : 2;           // output rows per thread
@@ -40,14 +46,18 @@ struct StackGeom {
   static constexpr int LANES = 32 * G;                 // planes / channels per stage
   static constexpr int Q = (S + 3) / 4;                // x-quads per row
   static constexpr int F_FLOATS = S * Q * LANES * 4;   // expanded fp32 stage
-  static constexpr int MIN_BLOCKS = (S == 7) ? 4 : (S == 14 ? 2 : 1);
+  static constexpr int MIN_BLOCKS = (S == 7) ? 4 : (S == 14 ? (MIX ? 3 : 2) : 1);
 };
+
+// 16-bit stacks compute from the raw stage with mixed-precision FMAs.
+template <typename T>
+constexpr bool kMixStack = sizeof(T) == 2;
 
 template <typename T, int S>
 struct StackSmem {
-  using G = StackGeom<S>;
+  using G = StackGeom<S, kMixStack<T>>;
   static constexpr uint32_t RAW = ((G::LANES * S * S * sizeof(T)) + 127u) & ~127u;
-  static constexpr uint32_t F_BYTES = G::F_FLOATS * sizeof(float);
+  static constexpr uint32_t F_BYTES = kMixStack<T> ? 0u : G::F_FLOATS * sizeof(float);
   static constexpr uint32_t OFF_F = 0;
   static constexpr uint32_t OFF_RAW = F_BYTES;
   static constexpr uint32_t OFF_BAR = OFF_RAW + 2 * RAW;
@@ -119,10 +129,11 @@ __device__ __forceinline__ float raw_to_f(__nv_bfloat16 v) { return __bfloat162f
 __device__ __forceinline__ float raw_to_f(__half v) { return __half2float(v); }
 
 template <typename T, bool NHWC, int S>
-__global__ void __launch_bounds__(StackGeom<S>::THREADS, StackGeom<S>::MIN_BLOCKS)
+__global__ void __launch_bounds__(StackGeom<S, kMixStack<T>>::THREADS, StackGeom<S, kMixStack<T>>::MIN_BLOCKS)
     stack_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap ymap,
                  const StackArgs a) {
-  using G = StackGeom<S>;
+  constexpr bool MIX = kMixStack<T>;
+  using G = StackGeom<S, MIX>;
   using M = StackSmem<T, S>;
   constexpr int R = G::R, Q = G::Q, LANES = G::LANES;
   extern __shared__ __align__(128) unsigned char smem[];
@@ -176,6 +187,7 @@ __global__ void __launch_bounds__(StackGeom<S>::THREADS, StackGeom<S>::MIN_BLOCK
   const T* wbase = static_cast<const T*>(a.w);
   const T* bbase = static_cast<const T*>(a.b);
   float wt[kTaps];
+  uint32_t wh[(kTaps + 1) / 2];
   int cur_c = -1;
   float bias = 0.f;
 
@@ -206,8 +218,12 @@ __global__ void __launch_bounds__(StackGeom<S>::THREADS, StackGeom<S>::MIN_BLOCK
     const int cw = lane_ok ? c : 0;
     if (cw != cur_c) {
       cur_c = cw;
+      if constexpr (MIX) {
+        load_taps16(wbase, cw, wh);
+      } else {
 #pragma unroll
-      for (int t = 0; t < kTaps; ++t) wt[t] = to_acc(wbase[cw * kTaps + t]);
+        for (int t = 0; t < kTaps; ++t) wt[t] = to_acc(wbase[cw * kTaps + t]);
+      }
       bias = bbase ? to_acc(bbase[cw]) : 0.f;
     }
 
@@ -225,26 +241,28 @@ __global__ void __launch_bounds__(StackGeom<S>::THREADS, StackGeom<S>::MIN_BLOCK
       mbar_wait_bounded(&bars[s], (it >> 1) & 1);
     }
 
-    // ---- widen to fp32, x-quad layout F[y][q][lane][4] -------------------
-    for (int i = tid; i < S * Q * LANES; i += G::THREADS) {
-      const int l = i % LANES;
-      const int yq = i / LANES;
-      const int yy = yq / Q, q = yq % Q;
-      float4 v;
-      float* vv = reinterpret_cast<float*>(&v);
+    // ---- fp32: widen / copy to the x-quad layout F[y][q][lane][4] --------------
+    if constexpr (!MIX) {
+      for (int i = tid; i < S * Q * LANES; i += G::THREADS) {
+        const int l = i % LANES;
+        const int yq = i / LANES;
+        const int yy = yq / Q, q = yq % Q;
+        float4 v;
+        float* vv = reinterpret_cast<float*>(&v);
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int xx = 4 * q + j;
-        float f = 0.f;
-        if (xx < S) {
-          const T e = NHWC ? rs[(yy * S + xx) * LANES + l] : rs[l * PLANE + yy * S + xx];
-          f = raw_to_f(e);
+        for (int j = 0; j < 4; ++j) {
+          const int xx = 4 * q + j;
+          float f = 0.f;
+          if (xx < S) {
+            const T e = NHWC ? rs[(yy * S + xx) * LANES + l] : rs[l * PLANE + yy * S + xx];
+            f = raw_to_f(e);
+          }
+          vv[j] = f;
         }
-        vv[j] = f;
+        reinterpret_cast<float4*>(F)[i] = v;
       }
-      reinterpret_cast<float4*>(F)[i] = v;
+      __syncthreads();
     }
-    __syncthreads();
 
     // ---- R output rows x S columns of plane `ln` -----------------------------
     float acc[R][S];
@@ -253,29 +271,72 @@ __global__ void __launch_bounds__(StackGeom<S>::THREADS, StackGeom<S>::MIN_BLOCK
 #pragma unroll
       for (int o = 0; o < S; ++o) acc[r][o] = 0.f;
 
-    const float4* F4 = reinterpret_cast<const float4*>(F) + ln;
+    if constexpr (MIX) {
+      const unsigned short* r16 = reinterpret_cast<const unsigned short*>(rs);
 #pragma unroll
-    for (int ir = 0; ir < R + 6; ++ir) {
-      const int iy = rg * R + ir - kHalo;
-      if (iy < 0 || iy >= S) continue;  // zero-padding row (warp-uniform)
-      float v[4 * Q];
+      for (int ir = 0; ir < R + 6; ++ir) {
+        const int iy = rg * R + ir - kHalo;
+        if (iy < 0 || iy >= S) continue;  // zero-padding row (warp-uniform)
+        unsigned short xv[S];           // row iy of plane / channel ln
+        if constexpr (NHWC) {
 #pragma unroll
-      for (int q = 0; q < Q; ++q) {
-        const float4 t = F4[(iy * Q + q) * LANES];
-        v[4 * q] = t.x; v[4 * q + 1] = t.y; v[4 * q + 2] = t.z; v[4 * q + 3] = t.w;
+          for (int xx = 0; xx < S; ++xx) xv[xx] = r16[(iy * S + xx) * LANES + ln];
+        } else if constexpr (S % 2 == 0) {
+          const uint32_t* p = reinterpret_cast<const uint32_t*>(r16 + ln * PLANE + iy * S);
+#pragma unroll
+          for (int q2 = 0; q2 < S / 2; ++q2) {
+            const uint32_t u = p[q2];
+            xv[2 * q2] = half_of(u, 0);
+            xv[2 * q2 + 1] = half_of(u, 1);
+          }
+        } else {  // odd-width rows are not word aligned
+#pragma unroll
+          for (int xx = 0; xx < S; ++xx) xv[xx] = r16[ln * PLANE + iy * S + xx];
+        }
+#pragma unroll
+        for (int kx = 0; kx < 7; ++kx) {
+#pragma unroll
+          for (int r = 0; r < R; ++r) {
+            const int ky = ir - r;
+            if (ky < 0 || ky >= 7) continue;
+            const int k = ky * 7 + kx;
+            const unsigned short wv = half_of(wh[k >> 1], k & 1);
+#pragma unroll
+            for (int o = 0; o < S; ++o) {
+              const int ix = o + kx - kHalo;
+              if (ix < 0 || ix >= S) continue;  // zero-padding column (compile time)
+              acc[r][o] = fma_mix(T(), xv[ix], wv, acc[r][o]);
+            }
+          }
+        }
       }
+      // Every row group is done reading the stage before outputs overwrite it.
+      __syncthreads();
+    } else {
+      const float4* F4 = reinterpret_cast<const float4*>(F) + ln;
 #pragma unroll
-      for (int kx = 0; kx < 7; ++kx) {
+      for (int ir = 0; ir < R + 6; ++ir) {
+        const int iy = rg * R + ir - kHalo;
+        if (iy < 0 || iy >= S) continue;  // zero-padding row (warp-uniform)
+        float v[4 * Q];
 #pragma unroll
-        for (int r = 0; r < R; ++r) {
-          const int ky = ir - r;
-          if (ky < 0 || ky >= 7) continue;
-          const float wv = wt[ky * 7 + kx];
+        for (int q = 0; q < Q; ++q) {
+          const float4 t = F4[(iy * Q + q) * LANES];
+          v[4 * q] = t.x; v[4 * q + 1] = t.y; v[4 * q + 2] = t.z; v[4 * q + 3] = t.w;
+        }
 #pragma unroll
-          for (int o = 0; o < S; ++o) {
-            const int ix = o + kx - kHalo;
-            if (ix < 0 || ix >= S) continue;  // zero-padding column (compile time)
-            acc[r][o] = fma_rn(v[ix], wv, acc[r][o]);
+        for (int kx = 0; kx < 7; ++kx) {
+#pragma unroll
+          for (int r = 0; r < R; ++r) {
+            const int ky = ir - r;
+            if (ky < 0 || ky >= 7) continue;
+            const float wv = wt[ky * 7 + kx];
+#pragma unroll
+            for (int o = 0; o < S; ++o) {
+              const int ix = o + kx - kHalo;
+              if (ix < 0 || ix >= S) continue;  // zero-padding column (compile time)
+              acc[r][o] = fma_rn(v[ix], wv, acc[r][o]);
+            }
           }
         }
       }

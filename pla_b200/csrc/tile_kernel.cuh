@@ -15,7 +15,11 @@
 //    (16-bit types) shared loads and applies it to every output row it
 //    touches (the 7-wide window is reused across the 4 columns in registers);
 //  * the 49 taps of the current plane's filter live in registers; fp32 FMA
-//    in row-major tap order; bias added in fp32; 128/64-bit vector stores.
+//    in row-major tap order; bias added in fp32; 128/64-bit vector stores;
+//  * 16-bit planes with device-resident filters take x and w straight from
+//    their packed 16-bit form into mixed-precision FMAs (fp32 accumulator,
+//    same bits as widening first), which drops the unpacking and halves the
+//    registers the taps need.
 #pragma once
 
 #include "pla_common.cuh"
@@ -146,7 +150,10 @@ __global__ void __launch_bounds__(kTileThreads, HOST_TAPS ? 5 : 4)
 
   const T* wt_base = static_cast<const T*>(a.w);
   const T* b_base = static_cast<const T*>(a.b);
+  // 16-bit planes, filter from device memory: packed 16-bit taps + mixed FMA.
+  constexpr bool MIX = sizeof(T) == 2 && !HOST_TAPS;
   float wt[kTaps];
+  uint32_t wh[(kTaps + 1) / 2];
   int cur_c = -1;
   float bias = 0.f;
 
@@ -163,8 +170,12 @@ __global__ void __launch_bounds__(kTileThreads, HOST_TAPS ? 5 : 4)
       const int c = plane - fdiv(plane, a.div_c) * a.C;
       if (c != cur_c) {
         cur_c = c;
+        if constexpr (MIX) {
+          load_taps16(wt_base, c, wh);
+        } else {
 #pragma unroll
-        for (int k = 0; k < kTaps; ++k) wt[k] = to_acc(wt_base[c * kTaps + k]);
+          for (int k = 0; k < kTaps; ++k) wt[k] = to_acc(wt_base[c * kTaps + k]);
+        }
         bias = b_base ? to_acc(b_base[c]) : 0.f;
       }
     }
@@ -178,23 +189,51 @@ __global__ void __launch_bounds__(kTileThreads, HOST_TAPS ? 5 : 4)
     // its accumulator with a plain product: RN(x * w) == fma(x, w, +0) except
     // for the sign of an exact zero, which no later "+" can tell apart.
     float acc[R][4];
+    if constexpr (MIX) {
+      // Same loop on packed 16-bit words: u[k / 2] half k & 1 is column ox - 4 + k.
+      // The first tap adds its product to -0, which returns RN(x * w) exactly.
 #pragma unroll
-    for (int ir = 0; ir < R + 6; ++ir) {
-      float v[12];
-      load_row12(s + ir * G::PITCH, v);
+      for (int ir = 0; ir < R + 6; ++ir) {
+        const uint2 q0 = *reinterpret_cast<const uint2*>(s + ir * G::PITCH);
+        const uint2 q1 = *reinterpret_cast<const uint2*>(s + ir * G::PITCH + 4);
+        const uint2 q2 = *reinterpret_cast<const uint2*>(s + ir * G::PITCH + 8);
+        const uint32_t u[6] = {q0.x, q0.y, q1.x, q1.y, q2.x, q2.y};
 #pragma unroll
-      for (int kx = 0; kx < 7; ++kx) {
+        for (int kx = 0; kx < 7; ++kx) {
 #pragma unroll
-        for (int r = 0; r < R; ++r) {
-          const int ky = ir - r;
-          if (ky >= 0 && ky < 7) {
-            const float wv = HOST_TAPS ? taps.w[ky * 7 + kx] : wt[ky * 7 + kx];
+          for (int r = 0; r < R; ++r) {
+            const int ky = ir - r;
+            if (ky >= 0 && ky < 7) {
+              const int k = ky * 7 + kx;
+              const unsigned short wv = half_of(wh[k >> 1], k & 1);
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              if (ky == 0 && kx == 0)
-                acc[r][j] = __fmul_rn(v[j + kx + 1], wv);
-              else
-                acc[r][j] = fma_rn(v[j + kx + 1], wv, acc[r][j]);
+              for (int j = 0; j < 4; ++j) {
+                const int c = j + kx + 1;
+                acc[r][j] = fma_mix(T(), half_of(u[c >> 1], c & 1), wv, (ky == 0 && kx == 0) ? -0.0f : acc[r][j]);
+              }
+            }
+          }
+        }
+      }
+    } else {
+#pragma unroll
+      for (int ir = 0; ir < R + 6; ++ir) {
+        float v[12];
+        load_row12(s + ir * G::PITCH, v);
+#pragma unroll
+        for (int kx = 0; kx < 7; ++kx) {
+#pragma unroll
+          for (int r = 0; r < R; ++r) {
+            const int ky = ir - r;
+            if (ky >= 0 && ky < 7) {
+              const float wv = HOST_TAPS ? taps.w[ky * 7 + kx] : wt[ky * 7 + kx];
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                if (ky == 0 && kx == 0)
+                  acc[r][j] = __fmul_rn(v[j + kx + 1], wv);
+                else
+                  acc[r][j] = fma_rn(v[j + kx + 1], wv, acc[r][j]);
+              }
             }
           }
         }

@@ -373,3 +373,43 @@ def test_misaligned_inputs_take_the_fallbacks(dtype, shape, layout):
         xs = xd[:, :1]
         ys = stencil7x7(xs, w[0:1].to(DEV), b[0:1].to(DEV))
         _assert_equal(ys, oracle.stencil7x7(x[:, :1].contiguous(), w[0:1], b[0:1]))
+
+
+def _with_specials(x: torch.Tensor, seed: int) -> torch.Tensor:
+    """x with a sprinkling of +-inf, NaN, -0 and subnormals of its own dtype."""
+    g = torch.Generator().manual_seed(seed)
+    flat = x.clone().reshape(-1)
+    n = flat.numel()
+    tiny = torch.finfo(x.dtype).tiny
+    picks = torch.randint(0, n, (5, max(1, n // 500)), generator=g)
+    flat[picks[0]] = float("inf")
+    flat[picks[1]] = float("-inf")
+    flat[picks[2]] = float("nan")
+    flat[picks[3]] = -0.0
+    flat[picks[4]] = tiny / 4  # subnormal
+    return flat.reshape(x.shape)
+
+
+def _assert_equal_nan(gpu: torch.Tensor, ref: torch.Tensor):
+    got = gpu.cpu()
+    assert torch.equal(torch.isnan(got), torch.isnan(ref)), "NaN positions differ"
+    keep = ~torch.isnan(ref)
+    _assert_equal(got[keep], ref[keep])
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("shape,layout", [((4, 64, 14, 14), "nchw"), ((4, 64, 14, 14), "nhwc"),
+                                          ((2, 64, 7, 7), "nchw"), ((2, 64, 28, 28), "nchw"),
+                                          ((1, 4, 56, 56), "nchw"), ((1, 2, 100, 300), "nchw")])
+def test_16bit_paths_with_special_values(dtype, shape, layout):
+    """The 16-bit kernels feed packed x and w into mixed-precision FMAs; infinities,
+    NaNs, signed zeros and subnormals must come out where the widened fp32 math
+    of the oracle puts them."""
+    from pla_b200 import depthwise7x7
+
+    x, w, b = _dw_inputs(21, shape, dtype, True)
+    x = _with_specials(x, 22)
+    fmt = torch.channels_last if layout == "nhwc" else torch.contiguous_format
+    x = x.contiguous(memory_format=fmt)
+    y = depthwise7x7(x.to(DEV), w.to(DEV), b.to(DEV))
+    _assert_equal_nan(y, oracle.depthwise7x7(x, w, b))
