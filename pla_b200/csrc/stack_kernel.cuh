@@ -26,9 +26,11 @@
 //    branch for rows): they would add an exact 0, so the fixed (ky, kx) tap
 //    order and hence the bits of every output are unchanged, while 23% (S=14)
 //    to 43% (S=7) of the FMAs of a padded formulation disappear.
-//  * Store: + bias in fp32, one rounding, written back into the stage's raw
-//    buffer (now free) in the source layout and sent out with one bulk copy /
-//    TMA store.
+//  * Store: + bias in fp32, one rounding, written in the source layout and
+//    sent out with one bulk copy / TMA store.  fp32 stacks reuse the stage's
+//    raw buffer (free once F holds it); 16-bit stacks, which read the raw
+//    buffer while computing, write to a 2-buffer output ring instead, so one
+//    barrier per stage suffices.
 #pragma once
 
 #include "pla_common.cuh"
@@ -60,7 +62,9 @@ struct StackSmem {
   static constexpr uint32_t F_BYTES = kMixStack<T> ? 0u : G::F_FLOATS * sizeof(float);
   static constexpr uint32_t OFF_F = 0;
   static constexpr uint32_t OFF_RAW = F_BYTES;
-  static constexpr uint32_t OFF_BAR = OFF_RAW + 2 * RAW;
+  // 16-bit stacks write outputs to their own 2-buffer ring (no in-place reuse).
+  static constexpr uint32_t OFF_OUT = OFF_RAW + 2 * RAW;
+  static constexpr uint32_t OFF_BAR = OFF_OUT + (kMixStack<T> ? 2 * RAW : 0u);
   static constexpr uint32_t TOTAL = OFF_BAR + 2 * sizeof(uint64_t);
 };
 
@@ -140,6 +144,7 @@ __global__ void __launch_bounds__(StackGeom<S, kMixStack<T>>::THREADS, StackGeom
   float* F = reinterpret_cast<float*>(smem + M::OFF_F);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + M::OFF_BAR);
   auto raw = [&](int s) { return reinterpret_cast<T*>(smem + M::OFF_RAW + s * M::RAW); };
+  auto outb = [&](int s) { return MIX ? reinterpret_cast<T*>(smem + M::OFF_OUT + s * M::RAW) : raw(s); };
 
   const int tid = threadIdx.x;
   const int lane = tid & 31;
@@ -195,7 +200,7 @@ __global__ void __launch_bounds__(StackGeom<S, kMixStack<T>>::THREADS, StackGeom
     const int s = it & 1;
     const int k = stage_of(v, a);
     if (tid == 0 && v + 1 < v_end) {
-      bulk_wait_read_all();  // raw[s^1] carried the previous stage's output
+      if (!MIX) bulk_wait_read_all();  // raw[s^1] carried the previous stage's output
       issue(stage_of(v + 1, a), s ^ 1);
     }
 
@@ -310,8 +315,6 @@ __global__ void __launch_bounds__(StackGeom<S, kMixStack<T>>::THREADS, StackGeom
           }
         }
       }
-      // Every row group is done reading the stage before outputs overwrite it.
-      __syncthreads();
     } else {
       const float4* F4 = reinterpret_cast<const float4*>(F) + ln;
 #pragma unroll
@@ -342,7 +345,9 @@ __global__ void __launch_bounds__(StackGeom<S, kMixStack<T>>::THREADS, StackGeom
       }
     }
 
-    // ---- + bias, round, stage the output in raw[s] (its input is consumed) ----
+    // ---- + bias, round, stage the output (fp32: in raw[s], whose input is
+    // consumed; 16-bit: in out[s], whose last bulk store has been read) ----
+    T* os = outb(s);
     const bool has_bias = bbase != nullptr;
 #pragma unroll
     for (int r = 0; r < R; ++r) {
@@ -354,24 +359,27 @@ __global__ void __launch_bounds__(StackGeom<S, kMixStack<T>>::THREADS, StackGeom
         if (has_bias) val += bias;
         const T e = from_acc<T>(val);
         if (NHWC)
-          rs[(oy * S + o) * LANES + ln] = e;
+          os[(oy * S + o) * LANES + ln] = e;
         else
-          rs[ln * PLANE + oy * S + o] = e;
+          os[ln * PLANE + oy * S + o] = e;
       }
     }
     fence_proxy_async_smem();
+    // 16-bit: before this barrier releases the next stage's writes into
+    // out[s ^ 1], the bulk store that read it (issued one stage ago) is done.
+    if (MIX && tid == 0) bulk_wait_read_all();
     __syncthreads();
 
     if (partial) {
       const long long base = static_cast<long long>(k) * LANES * PLANE;
       const long long left = (a.planes - static_cast<long long>(k) * LANES) * PLANE;
-      for (int i = tid; i < LANES * PLANE && i < left; i += G::THREADS) y[base + i] = rs[i];
+      for (int i = tid; i < LANES * PLANE && i < left; i += G::THREADS) y[base + i] = os[i];
     } else if (tid == 0) {
       if (NHWC) {
         const int cg = k - n_img * a.cgroups;
-        tma_store_4d(&ymap, rs, cg * LANES, 0, 0, n_img);
+        tma_store_4d(&ymap, os, cg * LANES, 0, 0, n_img);
       } else {
-        bulk_store(y + static_cast<long long>(k) * LANES * PLANE, rs, STAGE_BYTES);
+        bulk_store(y + static_cast<long long>(k) * LANES * PLANE, os, STAGE_BYTES);
       }
       bulk_commit();
     }
