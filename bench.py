@@ -17,6 +17,9 @@ one JSON line.  Workloads (the benchmark configurations; synthetic seeded inputs
                  over the GPUs (weak in the sense of fixed total work: strong)
   iterate_cfg5   one Jacobi step of the 32768^2 fp32 grid, row bands over the
                  GPUs with a 3-row halo exchange (strong scaling)
+  dw_k3          3x3 depthwise fp32 1x32x1024x1024, no bias: the operator and
+                 input recipe of the reference's MetaSchedule benchmark
+                 (benchmark/MetaSchedule/depthwise_conv.py, common.py)
 
 A "step" is one pass of the hot path over one batch of input already resident
 in HBM; consecutive steps rotate over enough buffer sets that every step's
@@ -36,6 +39,7 @@ import sys
 import threading
 import time
 
+import numpy as np
 import torch
 import torch.distributed as dist
 
@@ -275,12 +279,16 @@ class DepthwiseBase:
     bias = True
     seed = 0
     torch_dtype = torch.float32
+    k = 7               # filter side
+    recipe = "normal"   # x ~ N(0,1), w ~ N(0,1/49), b ~ N(0,0.01), torch generator
+    cpu_kind = "reference"
 
     def __init__(self, rank, world, dev):
-        from pla_b200.depthwise import depthwise7x7
+        from pla_b200.depthwise import depthwise7x7, depthwise_kxk
 
         self.dev = dev
-        self._fn = depthwise7x7
+        self.taps = self.k * self.k
+        self._fn = depthwise7x7 if self.k == 7 else depthwise_kxk
         es = torch.tensor([], dtype=self.torch_dtype).element_size()
         self.items = []
         self.bytes = 0
@@ -288,15 +296,23 @@ class DepthwiseBase:
         per_set = 0
         for (N, C, H, W) in self.stages:
             n_local = self.local_batch(N, world, rank)
-            g = torch.Generator().manual_seed(self.seed)
-            x = torch.randn(N, C, H, W, generator=g)[self.batch_slice(N, world, rank)]
-            w = torch.randn(C, 1, 7, 7, generator=g) / 7
-            b = torch.randn(C, generator=g) * 0.1 if self.bias else None
+            if self.recipe == "uniform":
+                # benchmark/MetaSchedule/common.py:176-177: numpy default_rng(seed), x then w ~ U(-1, 1)
+                rng = np.random.default_rng(self.seed)
+                x = torch.from_numpy(rng.uniform(-1, 1, (N, C, H, W)).astype(np.float32))
+                x = x[self.batch_slice(N, world, rank)]
+                w = torch.from_numpy(rng.uniform(-1, 1, (C, 1, self.k, self.k)).astype(np.float32))
+                b = None
+            else:
+                g = torch.Generator().manual_seed(self.seed)
+                x = torch.randn(N, C, H, W, generator=g)[self.batch_slice(N, world, rank)]
+                w = torch.randn(C, 1, 7, 7, generator=g) / 7
+                b = torch.randn(C, generator=g) * 0.1 if self.bias else None
             x, w = x.to(self.torch_dtype), w.to(self.torch_dtype)
             b = None if b is None else b.to(self.torch_dtype)
             pts = n_local * C * H * W
             self.points += pts
-            self.bytes += compulsory_bytes(pts, pts, es, C * TAPS, C if self.bias else 0, es)
+            self.bytes += compulsory_bytes(pts, pts, es, C * self.taps, C if self.bias else 0, es)
             per_set += 2 * pts * es
             self.items.append((x, w, b))
         self.nsets = rotate_sets(per_set)
@@ -314,7 +330,7 @@ class DepthwiseBase:
         from pla_b200 import _lib
 
         L = _lib.lib()
-        self._call = L.pla_depthwise7x7_forward
+        self._call = L.pla_depthwise7x7_forward if self.k == 7 else L.pla_depthwise_forward
         stream = torch.cuda.current_stream(dev).cuda_stream
         code = _lib.DTYPE_CODE[self.torch_dtype]
         lay = _lib.PLA_NHWC if self.layout == "nhwc" else _lib.PLA_NCHW
@@ -323,8 +339,9 @@ class DepthwiseBase:
             per = []
             for (xs, ys, w, b) in self.dev_items:
                 N, C, H, W = xs[k].shape
+                shape = (N, C, H, W) if self.k == 7 else (N, C, H, W, self.k)
                 per.append((xs[k].data_ptr(), w.data_ptr(), None if b is None else b.data_ptr(), ys[k].data_ptr(),
-                            N, C, H, W, code, lay, stream))
+                            *shape, code, lay, stream))
             self._args.append(per)
 
     @staticmethod
@@ -412,7 +429,7 @@ class DepthwiseBase:
         mods = []
         for (x, w, b) in self.items:
             C = x.shape[1]
-            m = DepthwiseModel(C, 7, 1, 3, bias=b is not None).to(self.torch_dtype)
+            m = DepthwiseModel(C, self.k, 1, self.k // 2, bias=b is not None).to(self.torch_dtype)
             with torch.no_grad():
                 m.conv2d.weight.copy_(w)
                 if b is not None:
@@ -432,11 +449,29 @@ class DepthwiseBase:
             for (x, w, b) in self.items:
                 _, C, H, W = x.shape
                 pts = nimg * C * H * W
-                tot += compulsory_bytes(pts, pts, es, C * TAPS, C if b is not None else 0, es)
+                tot += compulsory_bytes(pts, pts, es, C * self.taps, C if b is not None else 0, es)
             return tot
 
+        if self.k != 7:
+            return run_rows, bytes_rows, nb, \
+                f"torch.nn.Conv2d(C,C,{self.k},padding={self.k // 2},groups=C) CPU forward, the operator of " \
+                f"benchmark/MetaSchedule/depthwise_conv.py (its own CPU check is numpy inside the reference " \
+                f"tree, its GPU path TVM; neither is on this host), {self.layout}"
         return run_rows, bytes_rows, nb, f"torch.nn.Conv2d(C,C,7,padding=3,groups=C) CPU forward " \
                                          f"(data/depthwise_conv_7x7.py Model), {self.layout}"
+
+
+class DwK3(DepthwiseBase):
+    """3x3 depthwise of the reference's MetaSchedule benchmark at its logged 1x32x1024x1024 shape."""
+
+    name = "depthwise3x3_metaschedule_1x32x1024x1024_f32"
+    dtype = "f32"
+    stages = [(1, 32, 1024, 1024)]
+    k = 3
+    bias = False
+    seed = 0
+    recipe = "uniform"
+    cpu_kind = "port"
 
 
 class DwCfg1(DepthwiseBase):
@@ -571,7 +606,7 @@ class IterateCfg5:
 
 
 WORKLOADS = {"stencil_cfg2": StencilCfg2, "dw_cfg1": DwCfg1, "dw_cfg3_nchw": DwCfg3Nchw,
-             "dw_cfg3_nhwc": DwCfg3Nhwc, "dw_cfg4": DwCfg4, "iterate_cfg5": IterateCfg5}
+             "dw_cfg3_nhwc": DwCfg3Nhwc, "dw_cfg4": DwCfg4, "iterate_cfg5": IterateCfg5, "dw_k3": DwK3}
 
 
 # ---------------------------------------------------------------------------
@@ -615,7 +650,8 @@ def time_cpu_reference(wl, budget_s: float, steps: int | None = None, warmup: in
     gbs = bytes_rows(rows) * len(times) / total / 1e9
     sample = f"{what}; {len(times)} calls of {rows} of {nrows} rows/images each, " \
              f"{total:.2f} s, {threads} threads"
-    return gbs, {"value": gbs, "unit": "GB/s", "cores": torch.get_num_threads(), "kind": "reference",
+    return gbs, {"value": gbs, "unit": "GB/s", "cores": torch.get_num_threads(),
+                 "kind": getattr(wl, "cpu_kind", "reference"),
                  "sample": sample, "s_per_call": total / len(times)}
 
 
@@ -745,7 +781,8 @@ def main():
         kernel_ms = dom_ms
         kernel_what = f"launch of stage {list(dx.shape)} (the step's largest), CUDA events in the timed region"
     sm_mhz = clocks.get("sm_mhz") or 1965
-    fma_gpts = torch.cuda.get_device_properties(dev).multi_processor_count * FMA_PER_SM_PER_CLK * sm_mhz * 1e6 / TAPS / 1e9
+    fma_gpts = torch.cuda.get_device_properties(dev).multi_processor_count * FMA_PER_SM_PER_CLK * sm_mhz * 1e6 \
+        / getattr(wl, "taps", TAPS) / 1e9
 
     traffic, traffic_src = profiled_traffic(wl.name)
     cpu_baseline = None

@@ -126,6 +126,24 @@ PLA_API int pla_depthwise7x7_forward(const void* x, const void* w, const void* b
                              int dtype, int layout, pla_stream_t stream);
 
 /*
+ * Depthwise k x k convolution, k in {3, 5, 7} (groups = C, stride 1,
+ * padding k / 2), w [C,1,k,k], same arguments otherwise.  k = 7 is
+ * pla_depthwise7x7_forward.
+ *
+ * Replaces the operator of the reference's MetaSchedule benchmark
+ *   benchmark/MetaSchedule/depthwise_conv.py:7-13 and :32-33
+ *   (topi.nn.depthwise_conv2d_nchw(X, W, 1, k // 2, 1), kernel 3 or 7,
+ *    NCHW, no bias, fp32/fp16/bf16),
+ * whose numpy check (:41-46) accumulates the k*k products in fp32 in
+ * row-major (ry, rx) order.  Here every output is one fp32 FMA chain in that
+ * order plus the optional bias, rounded once; NHWC, bias and fp64 are also
+ * accepted.  Other k: PLA_ERR_UNSUPPORTED.
+ */
+PLA_API int pla_depthwise_forward(const void* x, const void* w, const void* b, void* y,
+                                  int n, int c, int h, int width, int k,
+                                  int dtype, int layout, pla_stream_t stream);
+
+/*
  * Iterated stencil on one device (no reference counterpart; the reference
  * path is data/stencil_7x7.py:10-12 applied `steps` times with zero padding
  * each step, i.e. a zero Dirichlet boundary):

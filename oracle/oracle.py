@@ -53,6 +53,10 @@ def _load():
         lib.oracle_depthwise7x7.restype = i32
         lib.oracle_depthwise7x7_f64.argtypes = [vp, vp, vp, vp, i32, i32, i32, i32, i32]
         lib.oracle_depthwise7x7_f64.restype = i32
+        lib.oracle_depthwise.argtypes = [vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, i32, i64, i64, i32, i32]
+        lib.oracle_depthwise.restype = i32
+        lib.oracle_depthwise_f64.argtypes = [vp, vp, vp, vp, i32, i32, i32, i32, i32, i32]
+        lib.oracle_depthwise_f64.restype = i32
         _lib = lib
     return _lib
 
@@ -78,11 +82,23 @@ def depthwise7x7(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None = None
     channels_last).  ``rows=(r0, r1)`` computes only output rows [r0, r1) and
     leaves the other rows of the result zero.
     """
+    return depthwise(x, w, b, threads, rows, k=7)
+
+
+def depthwise(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None = None,
+              threads: int | None = None, rows: tuple[int, int] | None = None, k: int | None = None) -> torch.Tensor:
+    """Oracle depthwise k x k (k odd <= 7, pad k // 2, stride 1); k defaults to w.shape[-1].
+
+    Same conventions as depthwise7x7; the k = 3 / 5 cases restate the operator
+    of benchmark/MetaSchedule/depthwise_conv.py:32-33.
+    """
     lib = _load()
     assert x.device.type == "cpu" and x.dim() == 4
     x, layout = _layout_of(x)
     N, C, H, W = x.shape
-    w = w.detach().reshape(C, 49).to(x.dtype).contiguous()
+    K = int(k if k is not None else w.shape[-1])
+    assert K in (1, 3, 5, 7) and w.numel() == C * K * K
+    w = w.detach().reshape(C, K * K).to(x.dtype).contiguous()
     b = None if b is None else b.detach().reshape(C).to(x.dtype).contiguous()
     y = torch.zeros_like(x)
     if x.numel() == 0:
@@ -91,7 +107,7 @@ def depthwise7x7(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None = None
     bp = None if b is None else b.data_ptr()
     if x.dtype == torch.float64:
         assert rows is None
-        lib.oracle_depthwise7x7_f64(x.data_ptr(), w.data_ptr(), bp, y.data_ptr(), N, C, H, W, layout)
+        lib.oracle_depthwise_f64(x.data_ptr(), w.data_ptr(), bp, y.data_ptr(), N, C, H, W, K, layout)
         return y
     code = _DTYPE_CODE[x.dtype]
     planes = N * C
@@ -108,8 +124,8 @@ def depthwise7x7(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None = None
                 jobs.append((p, p + 1, a, min(r1, a + step)))
 
     def run(job):
-        return lib.oracle_depthwise7x7(x.data_ptr(), w.data_ptr(), bp, y.data_ptr(), N, C, H, W, code, layout,
-                                       job[0], job[1], job[2], job[3])
+        return lib.oracle_depthwise(x.data_ptr(), w.data_ptr(), bp, y.data_ptr(), N, C, H, W, K, code, layout,
+                                    job[0], job[1], job[2], job[3])
 
     if nthr == 1 or len(jobs) == 1:
         for j in jobs:

@@ -28,6 +28,12 @@
  * the agreement is within rounding, which tests/test_oracle.py pins against
  * golden vectors produced by the reference modules themselves.
  *
+ * The k x k variants (k = 3, 5) restate the operator of the reference's
+ * MetaSchedule benchmark, benchmark/MetaSchedule/depthwise_conv.py:32-33
+ * (topi.nn.depthwise_conv2d_nchw, stride 1, padding k // 2, no bias), in the
+ * same fixed order; its own numpy check (:41-46) sums the k*k products in fp32
+ * in the same (ry, rx) order with separate multiply and add.
+ *
  * Build: see oracle/Makefile (gcc -O2 -ffp-contract=off).
  */
 #include <math.h>
@@ -90,15 +96,16 @@ static inline void store_f(void* p, int64_t i, float v, int dtype) {
  * x[base + r*sh + c*sw].  Rows [0,H), columns [0,W).
  */
 static inline float point_f32(const void* x, int64_t base, int64_t sh, int64_t sw, int H, int W, const float* wt,
-                              int i, int j, int dtype) {
+                              int K, int i, int j, int dtype) {
   float acc = 0.0f;
-  for (int ky = 0; ky < 7; ++ky) {
-    const int r = i + ky - HALO;
+  const int half = K / 2;
+  for (int ky = 0; ky < K; ++ky) {
+    const int r = i + ky - half;
     if (r < 0 || r >= H) continue;
-    for (int kx = 0; kx < 7; ++kx) {
-      const int c = j + kx - HALO;
+    for (int kx = 0; kx < K; ++kx) {
+      const int c = j + kx - half;
       if (c < 0 || c >= W) continue;
-      acc = fmaf(load_f(x, base + (int64_t)r * sh + (int64_t)c * sw, dtype), wt[ky * 7 + kx], acc);
+      acc = fmaf(load_f(x, base + (int64_t)r * sh + (int64_t)c * sw, dtype), wt[ky * K + kx], acc);
     }
   }
   return acc;
@@ -112,9 +119,10 @@ static inline float point_f32(const void* x, int64_t base, int64_t sh, int64_t s
  * written, so disjoint ranges can run on separate threads (the Python
  * wrapper in oracle/oracle.py does that; ctypes drops the GIL per call).
  */
-int oracle_depthwise7x7(const void* x, const void* w, const void* b, void* y, int N, int C, int H, int W,
-                        int dtype, int layout, int64_t p0, int64_t p1, int row0, int row1) {
+int oracle_depthwise(const void* x, const void* w, const void* b, void* y, int N, int C, int H, int W, int K,
+                     int dtype, int layout, int64_t p0, int64_t p1, int row0, int row1) {
   if (dtype == ORACLE_F64) return -1;
+  if (K < 1 || K > 7 || (K & 1) == 0) return -2;
   if (row0 < 0) row0 = 0;
   if (row1 > H) row1 = H;
   const int64_t plane = (int64_t)H * W;
@@ -124,7 +132,7 @@ int oracle_depthwise7x7(const void* x, const void* w, const void* b, void* y, in
   for (int64_t p = p0; p < p1; ++p) {
     const int n = (int)(p / C), ch = (int)(p % C);
     float wt[TAPS];
-    for (int k = 0; k < TAPS; ++k) wt[k] = load_f(w, (int64_t)ch * TAPS + k, dtype);
+    for (int k = 0; k < K * K; ++k) wt[k] = load_f(w, (int64_t)ch * K * K + k, dtype);
     const float bias = b ? load_f(b, ch, dtype) : 0.0f;
     int64_t base, sh, sw;
     if (layout == ORACLE_NCHW) {
@@ -138,7 +146,7 @@ int oracle_depthwise7x7(const void* x, const void* w, const void* b, void* y, in
     }
     for (int i = row0; i < row1; ++i)
       for (int j = 0; j < W; ++j) {
-        float acc = point_f32(x, base, sh, sw, H, W, wt, i, j, dtype);
+        float acc = point_f32(x, base, sh, sw, H, W, wt, K, i, j, dtype);
         if (b) acc = acc + bias;
         store_f(y, base + (int64_t)i * sh + (int64_t)j * sw, acc, dtype);
       }
@@ -146,9 +154,17 @@ int oracle_depthwise7x7(const void* x, const void* w, const void* b, void* y, in
   return 0;
 }
 
-/* fp64 variant (fp64 accumulation), NCHW or NHWC. */
-int oracle_depthwise7x7_f64(const double* x, const double* w, const double* b, double* y, int N, int C, int H,
-                            int W, int layout) {
+/* The 7x7 case (data/depthwise_conv_7x7.py, data/stencil_7x7.py). */
+int oracle_depthwise7x7(const void* x, const void* w, const void* b, void* y, int N, int C, int H, int W,
+                        int dtype, int layout, int64_t p0, int64_t p1, int row0, int row1) {
+  return oracle_depthwise(x, w, b, y, N, C, H, W, 7, dtype, layout, p0, p1, row0, row1);
+}
+
+/* fp64 variant (fp64 accumulation), k x k, NCHW or NHWC. */
+int oracle_depthwise_f64(const double* x, const double* w, const double* b, double* y, int N, int C, int H, int W,
+                         int K, int layout) {
+  if (K < 1 || K > 7 || (K & 1) == 0) return -2;
+  const int half = K / 2;
   const int64_t plane = (int64_t)H * W;
   const int64_t planes = (int64_t)N * C;
   for (int64_t p = 0; p < planes; ++p) {
@@ -166,13 +182,13 @@ int oracle_depthwise7x7_f64(const double* x, const double* w, const double* b, d
     for (int i = 0; i < H; ++i)
       for (int j = 0; j < W; ++j) {
         double acc = 0.0;
-        for (int ky = 0; ky < 7; ++ky) {
-          const int r = i + ky - HALO;
+        for (int ky = 0; ky < K; ++ky) {
+          const int r = i + ky - half;
           if (r < 0 || r >= H) continue;
-          for (int kx = 0; kx < 7; ++kx) {
-            const int c = j + kx - HALO;
+          for (int kx = 0; kx < K; ++kx) {
+            const int c = j + kx - half;
             if (c < 0 || c >= W) continue;
-            acc = fma(x[base + r * sh + c * sw], w[(int64_t)ch * TAPS + ky * 7 + kx], acc);
+            acc = fma(x[base + r * sh + c * sw], w[(int64_t)ch * K * K + ky * K + kx], acc);
           }
         }
         if (b) acc = acc + b[ch];
@@ -180,6 +196,11 @@ int oracle_depthwise7x7_f64(const double* x, const double* w, const double* b, d
       }
   }
   return 0;
+}
+
+int oracle_depthwise7x7_f64(const double* x, const double* w, const double* b, double* y, int N, int C, int H,
+                            int W, int layout) {
+  return oracle_depthwise_f64(x, w, b, y, N, C, H, W, 7, layout);
 }
 
 /*

@@ -3,8 +3,9 @@
 // Covers what the fast kernels do not: non-contiguous or misaligned stencil
 // inputs (the strided cases of data/stencil_direct_cuda_v7/test_stencil.py:31-37:
 // sliced, transposed and batch-sliced tensors), fp64, and depthwise shapes
-// whose rows break the vector-alignment rules.  One thread per output point,
-// the same tap order and rounding as the fast kernels.
+// whose rows break the vector-alignment rules, and depthwise filters of any
+// odd size K <= 7 in any layout.  One thread per output point, the same tap
+// order and rounding as the fast kernels.
 #pragma once
 
 #include "pla_common.cuh"
@@ -13,13 +14,14 @@ namespace pla {
 
 struct GenericArgs {
   const void* x;
-  const void* w;  // [C][49]
+  const void* w;  // [C][K*K]
   const void* b;  // [C] or nullptr
   void* y;
   int N, C, H, W;
   long long xs_n, xs_c, xs_h, xs_w;  // input element strides
   long long ys_n, ys_c, ys_h, ys_w;  // output element strides
   long long total;                   // N*C*H*W
+  int K;                             // filter side (odd, <= 7); padding K / 2
 };
 
 template <typename T>
@@ -38,15 +40,16 @@ __global__ void __launch_bounds__(256) generic_kernel(const GenericArgs a) {
     const int c = static_cast<int>(q % a.C);
     const int n = static_cast<int>(q / a.C);
     const T* xp = x + n * a.xs_n + c * a.xs_c;
-    const T* wp = w + static_cast<long long>(c) * kTaps;
+    const int K = a.K, half = a.K / 2;
+    const T* wp = w + static_cast<long long>(c) * K * K;
     Acc acc = Acc(0);
-    for (int ky = 0; ky < 7; ++ky) {
-      const int yy = Y + ky - kHalo;
+    for (int ky = 0; ky < K; ++ky) {
+      const int yy = Y + ky - half;
       if (yy < 0 || yy >= a.H) continue;
-      for (int kx = 0; kx < 7; ++kx) {
-        const int xx = X + kx - kHalo;
+      for (int kx = 0; kx < K; ++kx) {
+        const int xx = X + kx - half;
         if (xx < 0 || xx >= a.W) continue;
-        acc = fma_rn(to_acc(xp[yy * a.xs_h + xx * a.xs_w]), to_acc(wp[ky * 7 + kx]), acc);
+        acc = fma_rn(to_acc(xp[yy * a.xs_h + xx * a.xs_w]), to_acc(wp[ky * K + kx]), acc);
       }
     }
     if (b) acc += to_acc(b[c]);

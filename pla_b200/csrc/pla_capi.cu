@@ -182,22 +182,27 @@ bool tile_path_ok(const void* x, const void* y, int dtype, int width, long long 
   return true;
 }
 
-template <typename T, int R, int LX>
+template <typename T, int R, int LX, int K = 7>
 int launch_tile(const void* x, const void* w, const void* b, const HostTaps* ht, void* y, int dtype, int planes,
                 int C, int in_rows, int width, long long x_row_stride, long long x_plane_stride, int row_begin,
                 int row_end, int in_row_shift, long long y_plane_stride, long long y_row_stride,
                 cudaStream_t stream) {
-  using G = TileGeom<T, R, LX>;
+  using G = TileGeom<T, R, LX, K>;
   int st;
   DeviceInfo* d = device_info(&st);
   if (!d) return st;
   if (row_end <= row_begin || planes == 0 || width == 0) return PLA_OK;
+  if (K != 7 && ht) return PLA_ERR_UNSUPPORTED;  // host taps hold a 7x7 filter
   CUtensorMap map;
   st = make_tile_map<T, G>(&map, x, dtype, width, in_rows, planes, x_row_stride, x_plane_stride);
   if (st != PLA_OK) return st;
   int per_sm = 1;
-  st = ht ? kernel_setup<tile_kernel<T, R, LX, true>>(kTileThreads, G::SMEM, &per_sm)
-          : kernel_setup<tile_kernel<T, R, LX, false>>(kTileThreads, G::SMEM, &per_sm);
+  if constexpr (K == 7) {
+    st = ht ? kernel_setup<tile_kernel<T, R, LX, true>>(kTileThreads, G::SMEM, &per_sm)
+            : kernel_setup<tile_kernel<T, R, LX, false>>(kTileThreads, G::SMEM, &per_sm);
+  } else {
+    st = kernel_setup<tile_kernel<T, R, LX, false, false, K>>(kTileThreads, G::SMEM, &per_sm);
+  }
   if (st != PLA_OK) return st;
   TileArgs a;
   a.w = w;
@@ -222,30 +227,35 @@ int launch_tile(const void* x, const void* w, const void* b, const HostTaps* ht,
   const long long slots = static_cast<long long>(d->sms) * per_sm;
   const int grid = static_cast<int>(total < slots ? total : slots);
   const HaloLinks no_halo{};
-  if (ht) {
-    tile_kernel<T, R, LX, true><<<grid, kTileThreads, G::SMEM, stream>>>(map, a, *ht, no_halo);
+  if constexpr (K == 7) {
+    if (ht) {
+      tile_kernel<T, R, LX, true><<<grid, kTileThreads, G::SMEM, stream>>>(map, a, *ht, no_halo);
+    } else {
+      HostTaps unused{};
+      tile_kernel<T, R, LX, false><<<grid, kTileThreads, G::SMEM, stream>>>(map, a, unused, no_halo);
+    }
   } else {
     HostTaps unused{};
-    tile_kernel<T, R, LX, false><<<grid, kTileThreads, G::SMEM, stream>>>(map, a, unused, no_halo);
+    tile_kernel<T, R, LX, false, false, K><<<grid, kTileThreads, G::SMEM, stream>>>(map, a, unused, no_halo);
   }
   PLA_CUDA(cudaGetLastError());
   return PLA_OK;
 }
 
-template <typename T>
+template <typename T, int K = 7>
 int launch_tile_shape(int shape, const void* x, const void* w, const void* b, const HostTaps* ht, void* y,
                       int dtype, int planes, int C, int in_rows, int width, long long x_row_stride,
                       long long x_plane_stride, int row_begin, int row_end, int in_row_shift,
                       long long y_plane_stride, long long y_row_stride, cudaStream_t stream) {
   if (shape == 1)
-    return launch_tile<T, kNarrowR, kNarrowLX>(x, w, b, ht, y, dtype, planes, C, in_rows, width, x_row_stride,
+    return launch_tile<T, kNarrowR, kNarrowLX, K>(x, w, b, ht, y, dtype, planes, C, in_rows, width, x_row_stride,
                                                x_plane_stride, row_begin, row_end, in_row_shift, y_plane_stride,
                                                y_row_stride, stream);
   if (shape == 2)
-    return launch_tile<T, kShortR, kNarrowLX>(x, w, b, ht, y, dtype, planes, C, in_rows, width, x_row_stride,
+    return launch_tile<T, kShortR, kNarrowLX, K>(x, w, b, ht, y, dtype, planes, C, in_rows, width, x_row_stride,
                                               x_plane_stride, row_begin, row_end, in_row_shift, y_plane_stride,
                                               y_row_stride, stream);
-  return launch_tile<T, kWideR, kWideLX>(x, w, b, ht, y, dtype, planes, C, in_rows, width, x_row_stride,
+  return launch_tile<T, kWideR, kWideLX, K>(x, w, b, ht, y, dtype, planes, C, in_rows, width, x_row_stride,
                                          x_plane_stride, row_begin, row_end, in_row_shift, y_plane_stride,
                                          y_row_stride, stream);
 }
@@ -253,6 +263,7 @@ int launch_tile_shape(int shape, const void* x, const void* w, const void* b, co
 // Narrow tiles only pay off for 33..64-wide planes tall enough to fill them.
 bool use_narrow_tiles(int width, int rows) { return width > 32 && width <= 64 && rows > 28; }
 
+template <int K = 7>
 int launch_tile_dtype(int dtype, const void* x, const void* w, const void* b, const HostTaps* ht, void* y,
                       int planes, int C, int in_rows, int width, long long x_row_stride, long long x_plane_stride,
                       int row_begin, int row_end, int in_row_shift, long long y_plane_stride,
@@ -269,15 +280,15 @@ int launch_tile_dtype(int dtype, const void* x, const void* w, const void* b, co
   }
   switch (dtype) {
     case PLA_F32:
-      return launch_tile_shape<float>(narrow, x, w, b, ht, y, dtype, planes, C, in_rows, width, x_row_stride,
+      return launch_tile_shape<float, K>(narrow, x, w, b, ht, y, dtype, planes, C, in_rows, width, x_row_stride,
                                       x_plane_stride, row_begin, row_end, in_row_shift, y_plane_stride,
                                       y_row_stride, stream);
     case PLA_BF16:
-      return launch_tile_shape<__nv_bfloat16>(narrow, x, w, b, ht, y, dtype, planes, C, in_rows, width,
+      return launch_tile_shape<__nv_bfloat16, K>(narrow, x, w, b, ht, y, dtype, planes, C, in_rows, width,
                                               x_row_stride, x_plane_stride, row_begin, row_end, in_row_shift,
                                               y_plane_stride, y_row_stride, stream);
     case PLA_F16:
-      return launch_tile_shape<__half>(narrow, x, w, b, ht, y, dtype, planes, C, in_rows, width, x_row_stride,
+      return launch_tile_shape<__half, K>(narrow, x, w, b, ht, y, dtype, planes, C, in_rows, width, x_row_stride,
                                        x_plane_stride, row_begin, row_end, in_row_shift, y_plane_stride,
                                        y_row_stride, stream);
     default:
@@ -573,6 +584,7 @@ int stencil_forward_impl(const void* x, const void* w, const void* b, const Host
   a.xs_n = sn; a.xs_c = 0; a.xs_h = sh; a.xs_w = sw;
   a.ys_n = plane; a.ys_c = 0; a.ys_h = width; a.ys_w = 1;
   a.total = static_cast<long long>(n) * plane;
+  a.K = 7;
   return launch_generic_dtype(dtype, a, s);
 }
 
@@ -720,6 +732,44 @@ int pla_depthwise7x7_forward(const void* x, const void* w, const void* b, void* 
   }
   a.ys_n = a.xs_n; a.ys_c = a.xs_c; a.ys_h = a.xs_h; a.ys_w = a.xs_w;
   a.total = planes * plane;
+  a.K = 7;
+  return launch_generic_dtype(dtype, a, s);
+}
+
+int pla_depthwise_forward(const void* x, const void* w, const void* b, void* y, int n, int c, int h, int width,
+                          int k, int dtype, int layout, pla_stream_t stream) {
+  if (k == 7) return pla_depthwise7x7_forward(x, w, b, y, n, c, h, width, dtype, layout, stream);
+  if (k != 3 && k != 5) return PLA_ERR_UNSUPPORTED;
+  if (!valid_dtype(dtype)) return PLA_ERR_UNSUPPORTED;
+  if (layout != PLA_NCHW && layout != PLA_NHWC) return PLA_ERR_INVALID_ARGUMENT;
+  if (n < 0 || c < 0 || h < 0 || width < 0) return PLA_ERR_INVALID_ARGUMENT;
+  if (static_cast<long long>(n) * c * h * width == 0) return PLA_OK;
+  if (!x || !w || !y) return PLA_ERR_INVALID_ARGUMENT;
+  if (h > (1 << 30) || width > (1 << 30)) return PLA_ERR_TOO_LARGE;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const long long plane = static_cast<long long>(h) * width;
+  const long long planes = static_cast<long long>(n) * c;
+  // Dense NCHW planes wide enough for the tile shapes: the TMA tile kernel
+  // with a k x k filter.  Everything else (NHWC, small or misaligned planes,
+  // fp64): the one-thread-per-output kernel.
+  if (dtype != PLA_F64 && layout == PLA_NCHW && (width >= 64 || use_narrow_tiles(width, h)) &&
+      planes <= 0x7fffffffll && tile_path_ok(x, y, dtype, width, width, plane, static_cast<int>(planes))) {
+    return k == 3 ? launch_tile_dtype<3>(dtype, x, w, b, nullptr, y, static_cast<int>(planes), c, h, width, width,
+                                         plane, 0, h, 0, plane, width, s)
+                  : launch_tile_dtype<5>(dtype, x, w, b, nullptr, y, static_cast<int>(planes), c, h, width, width,
+                                         plane, 0, h, 0, plane, width, s);
+  }
+  GenericArgs a;
+  a.x = x; a.w = w; a.b = b; a.y = y;
+  a.N = n; a.C = c; a.H = h; a.W = width;
+  if (layout == PLA_NCHW) {
+    a.xs_n = c * plane; a.xs_c = plane; a.xs_h = width; a.xs_w = 1;
+  } else {
+    a.xs_n = c * plane; a.xs_c = 1; a.xs_h = static_cast<long long>(width) * c; a.xs_w = c;
+  }
+  a.ys_n = a.xs_n; a.ys_c = a.xs_c; a.ys_h = a.xs_h; a.ys_w = a.xs_w;
+  a.total = planes * plane;
+  a.K = k;
   return launch_generic_dtype(dtype, a, s);
 }
 

@@ -102,13 +102,13 @@ __device__ __forceinline__ unsigned short half_of(uint32_t w, int hi) {
   asm("mov.b32 {%0, %1}, %2;" : "=h"(l), "=h"(h) : "r"(w));
   return hi ? h : l;
 }
-// The 49 taps of filter c as packed 16-bit pairs: tap k in half k & 1 of p[k / 2].
-template <typename T>
-__device__ __forceinline__ void load_taps16(const T* w, int c, uint32_t (&p)[(kTaps + 1) / 2]) {
-  const unsigned short* wb = reinterpret_cast<const unsigned short*>(w) + c * kTaps;
+// The NT taps of filter c as packed 16-bit pairs: tap k in half k & 1 of p[k / 2].
+template <int NT, typename T>
+__device__ __forceinline__ void load_taps16(const T* w, int c, uint32_t (&p)[(NT + 1) / 2]) {
+  const unsigned short* wb = reinterpret_cast<const unsigned short*>(w) + c * NT;
 #pragma unroll
-  for (int k = 0; k < (kTaps + 1) / 2; ++k)
-    p[k] = static_cast<uint32_t>(wb[2 * k]) | (2 * k + 1 < kTaps ? static_cast<uint32_t>(wb[2 * k + 1]) << 16 : 0u);
+  for (int k = 0; k < (NT + 1) / 2; ++k)
+    p[k] = static_cast<uint32_t>(wb[2 * k]) | (2 * k + 1 < NT ? static_cast<uint32_t>(wb[2 * k + 1]) << 16 : 0u);
 }
 
 // ---------------------------------------------------------------------------

@@ -224,7 +224,7 @@ __global__ void __launch_bounds__(StackGeom<S, kMixStack<T>>::THREADS, StackGeom
     if (cw != cur_c) {
       cur_c = cw;
       if constexpr (MIX) {
-        load_taps16(wbase, cw, wh);
+        load_taps16<kTaps>(wbase, cw, wh);
       } else {
 #pragma unroll
         for (int t = 0; t < kTaps; ++t) wt[t] = to_acc(wbase[cw * kTaps + t]);

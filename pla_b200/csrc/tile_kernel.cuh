@@ -1,4 +1,5 @@
-// Plane-tile kernel: 7x7 correlation over a stack of dense planes
+// Plane-tile kernel: K x K correlation (K = 7; 3 and 5 for the depthwise
+// filters of the reference's MetaSchedule benchmark) over a stack of dense planes
 // (the single-step stencil of data/stencil_7x7.py, NCHW depthwise planes of
 // data/depthwise_conv_7x7.py with wide rows, and one Jacobi step of the
 // iterated stencil, whole grid or one row band).
@@ -7,7 +8,9 @@
 //  * persistent CTAs (grid = #SMs x resident CTAs) walk a flat list of
 //    TH x TW output tiles, plane-major then row-major;
 //  * each tile's (TH+6) x (TW+2*LEFT) input window is one 3-D TMA tile load
-//    (cp.async.bulk.tensor, no multicast) into a 2-stage shared-memory ring
+//    (cp.async.bulk.tensor, no multicast) into a shared-memory ring of NS = 2
+//    stages (3 or 4 stages measured slower for every filter size: the larger
+//    ring leaves room for fewer CTAs per SM)
 //    guarded by mbarriers, so the next tile streams in while this one is
 //    computed; TMA's out-of-bounds zero fill supplies the zero padding;
 //  * 4 warps; a thread owns R rows x 4 columns of outputs, loads
@@ -35,19 +38,20 @@ constexpr int kTileThreads = 128;
 // The TMA box starts LEFT columns left of the tile: LEFT * sizeof(T) == 16 B
 // keeps the innermost TMA coordinate 16-byte aligned (a hard TMA rule), and
 // LEFT >= 3 covers the halo.  The box is LEFT + TW + LEFT wide.
-template <typename T, int R, int LX>
+template <typename T, int R, int LX, int K = 7>
 struct TileGeom {
+  static constexpr int NS = 2;                          // ring stages
   static_assert(LX == 32 || LX == 16, "column groups per warp");
   static constexpr int TW = 4 * LX;                     // output columns per tile
   static constexpr int TH = (kTileThreads / 32) * (32 / LX) * R;  // output rows per tile
-  static constexpr int ROWS = TH + 6;        // input rows per tile (3-row halo)
+  static constexpr int ROWS = TH + K - 1;    // input rows per tile (K / 2-row halo)
   static constexpr int LEFT = 16 / sizeof(T);
   static constexpr int PITCH = TW + 2 * LEFT;
   static_assert(LEFT >= 4 && (LEFT * sizeof(T)) % 16 == 0, "TMA x must stay 16-byte aligned");
   static_assert((PITCH * sizeof(T)) % 16 == 0, "TMA box inner extent must be a multiple of 16 B");
   static constexpr uint32_t BYTES = ROWS * PITCH * sizeof(T);
   static constexpr uint32_t STAGE = (BYTES + 127u) & ~127u;
-  static constexpr uint32_t SMEM = 2 * STAGE + 2 * sizeof(uint64_t);
+  static constexpr uint32_t SMEM = NS * STAGE + NS * sizeof(uint64_t);
 };
 
 struct TileArgs {
@@ -102,13 +106,18 @@ __device__ __forceinline__ int halo_tile_row(int q, int tiles_y, int bot0) {
 // HOST_TAPS: one filter for every plane, read from the HostTaps parameter;
 // otherwise plane p uses the device filter a.w[(p % C) * 49 ...] held in
 // registers.
-template <typename T, int R, int LX, bool HOST_TAPS, bool HALO = false>
+template <typename T, int R, int LX, bool HOST_TAPS, bool HALO = false, int K = 7>
 __global__ void __launch_bounds__(kTileThreads, HOST_TAPS ? 5 : 4)
     tile_kernel(const __grid_constant__ CUtensorMap tmap, const TileArgs a,
                 const __grid_constant__ HostTaps taps, const __grid_constant__ HaloLinks h) {
-  using G = TileGeom<T, R, LX>;
+  static_assert(K == 3 || K == 5 || K == 7, "filter side");
+  static_assert(K == 7 || (!HALO && !HOST_TAPS), "halo exchange and host taps are 7x7 only");
+  constexpr int NT = K * K;        // taps
+  constexpr int CX = 4 - K / 2;    // v[j + kx + CX] is input column ox + j + kx - K / 2
+  using G = TileGeom<T, R, LX, K>;
   extern __shared__ __align__(128) unsigned char smem[];
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 2 * G::STAGE);
+  constexpr int NS = G::NS;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + NS * G::STAGE);
 
   const int tid = threadIdx.x;
   const int lane = tid & 31;
@@ -117,8 +126,8 @@ __global__ void __launch_bounds__(kTileThreads, HOST_TAPS ? 5 : 4)
 
   if (tid == 0) {
     prefetch_tensormap(&tmap);
-    mbar_init(&bars[0], 1);
-    mbar_init(&bars[1], 1);
+#pragma unroll
+    for (int i = 0; i < NS; ++i) mbar_init(&bars[i], 1);
     fence_mbar_init();
   }
   __syncthreads();
@@ -140,26 +149,33 @@ __global__ void __launch_bounds__(kTileThreads, HOST_TAPS ? 5 : 4)
       fence_proxy_async_global();
     }
     const int x0 = tx * G::TW - G::LEFT;
-    const int y0 = a.row_begin + ty * G::TH + a.in_row_shift - kHalo;
+    const int y0 = a.row_begin + ty * G::TH + a.in_row_shift - K / 2;
     fence_proxy_async_smem();
     mbar_arrive_expect_tx(&bars[stage], G::BYTES);
     tma_load_3d(smem + stage * G::STAGE, &tmap, &bars[stage], x0, y0, plane);
   };
 
-  if (tid == 0 && t < total) issue(t, 0);
+  // Prologue: the first NS - 1 tiles of this CTA.
+  if (tid == 0) {
+#pragma unroll
+    for (int j = 0; j < NS - 1; ++j)
+      if (t + j * stride < total) issue(t + j * stride, j);
+  }
 
   const T* wt_base = static_cast<const T*>(a.w);
   const T* b_base = static_cast<const T*>(a.b);
   // 16-bit planes, filter from device memory: packed 16-bit taps + mixed FMA.
   constexpr bool MIX = sizeof(T) == 2 && !HOST_TAPS;
-  float wt[kTaps];
-  uint32_t wh[(kTaps + 1) / 2];
+  float wt[NT];
+  uint32_t wh[(NT + 1) / 2];
   int cur_c = -1;
   float bias = 0.f;
 
   for (int it = 0; t < total; ++it, t += stride) {
-    const int stage = it & 1;
-    if (tid == 0 && t + stride < total) issue(t + stride, stage ^ 1);
+    const int stage = it % NS;
+    // Tile it + NS - 1 goes into the stage that tile it - 1 used; every
+    // thread left that stage at the barrier that ended iteration it - 1.
+    if (tid == 0 && t + (NS - 1) * stride < total) issue(t + (NS - 1) * stride, (it + NS - 1) % NS);
 
     const int q = fdiv(t, a.div_tx);
     const int tx = t - q * a.tiles_x;
@@ -171,16 +187,16 @@ __global__ void __launch_bounds__(kTileThreads, HOST_TAPS ? 5 : 4)
       if (c != cur_c) {
         cur_c = c;
         if constexpr (MIX) {
-          load_taps16(wt_base, c, wh);
+          load_taps16<NT>(wt_base, c, wh);
         } else {
 #pragma unroll
-          for (int k = 0; k < kTaps; ++k) wt[k] = to_acc(wt_base[c * kTaps + k]);
+          for (int k = 0; k < NT; ++k) wt[k] = to_acc(wt_base[c * NT + k]);
         }
         bias = b_base ? to_acc(b_base[c]) : 0.f;
       }
     }
 
-    mbar_wait_bounded(&bars[stage], (it >> 1) & 1);
+    mbar_wait_bounded(&bars[stage], (it / NS) & 1);
 
     // v[k] below is input column ox - 4 + k (ox = this thread's first output column).
     const T* s = reinterpret_cast<const T*>(smem + stage * G::STAGE) + (rgrp * R) * G::PITCH + 4 * cgrp +
@@ -193,22 +209,22 @@ __global__ void __launch_bounds__(kTileThreads, HOST_TAPS ? 5 : 4)
       // Same loop on packed 16-bit words: u[k / 2] half k & 1 is column ox - 4 + k.
       // The first tap adds its product to -0, which returns RN(x * w) exactly.
 #pragma unroll
-      for (int ir = 0; ir < R + 6; ++ir) {
+      for (int ir = 0; ir < R + K - 1; ++ir) {
         const uint2 q0 = *reinterpret_cast<const uint2*>(s + ir * G::PITCH);
         const uint2 q1 = *reinterpret_cast<const uint2*>(s + ir * G::PITCH + 4);
         const uint2 q2 = *reinterpret_cast<const uint2*>(s + ir * G::PITCH + 8);
         const uint32_t u[6] = {q0.x, q0.y, q1.x, q1.y, q2.x, q2.y};
 #pragma unroll
-        for (int kx = 0; kx < 7; ++kx) {
+        for (int kx = 0; kx < K; ++kx) {
 #pragma unroll
           for (int r = 0; r < R; ++r) {
             const int ky = ir - r;
-            if (ky >= 0 && ky < 7) {
-              const int k = ky * 7 + kx;
+            if (ky >= 0 && ky < K) {
+              const int k = ky * K + kx;
               const unsigned short wv = half_of(wh[k >> 1], k & 1);
 #pragma unroll
               for (int j = 0; j < 4; ++j) {
-                const int c = j + kx + 1;
+                const int c = j + kx + CX;
                 acc[r][j] = fma_mix(T(), half_of(u[c >> 1], c & 1), wv, (ky == 0 && kx == 0) ? -0.0f : acc[r][j]);
               }
             }
@@ -217,22 +233,22 @@ __global__ void __launch_bounds__(kTileThreads, HOST_TAPS ? 5 : 4)
       }
     } else {
 #pragma unroll
-      for (int ir = 0; ir < R + 6; ++ir) {
+      for (int ir = 0; ir < R + K - 1; ++ir) {
         float v[12];
         load_row12(s + ir * G::PITCH, v);
 #pragma unroll
-        for (int kx = 0; kx < 7; ++kx) {
+        for (int kx = 0; kx < K; ++kx) {
 #pragma unroll
           for (int r = 0; r < R; ++r) {
             const int ky = ir - r;
-            if (ky >= 0 && ky < 7) {
-              const float wv = HOST_TAPS ? taps.w[ky * 7 + kx] : wt[ky * 7 + kx];
+            if (ky >= 0 && ky < K) {
+              const float wv = HOST_TAPS ? taps.w[ky * K + kx] : wt[ky * K + kx];
 #pragma unroll
               for (int j = 0; j < 4; ++j) {
                 if (ky == 0 && kx == 0)
-                  acc[r][j] = __fmul_rn(v[j + kx + 1], wv);
+                  acc[r][j] = __fmul_rn(v[j + kx + CX], wv);
                 else
-                  acc[r][j] = fma_rn(v[j + kx + 1], wv, acc[r][j]);
+                  acc[r][j] = fma_rn(v[j + kx + CX], wv, acc[r][j]);
               }
             }
           }

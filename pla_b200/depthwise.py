@@ -12,6 +12,10 @@ bias=True), ``get_inputs()``, ``get_init_inputs()``.
 Beyond the reference kernels (fp16/fp32, NCHW, no bias, weights repacked to
 [C,8,80]): fp32 / bf16 / fp16 / fp64, NCHW and channels_last (NHWC), optional
 bias, and no weight repack (the kernels read the module's own weight).
+
+``depthwise_kxk()`` also takes 3x3 and 5x5 filters (padding k // 2): the operator
+of the reference's MetaSchedule benchmark
+(``benchmark/MetaSchedule/depthwise_conv.py:7-13, 32-33``, kernel 3 or 7).
 """
 from __future__ import annotations
 
@@ -35,6 +39,16 @@ def depthwise7x7(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | Non
     torch does); a contiguous input runs NCHW; anything else is made
     contiguous first.
     """
+    return depthwise_kxk(x, weight, bias, out, k=7)
+
+
+def depthwise_kxk(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None,
+              out: torch.Tensor | None = None, k: int | None = None) -> torch.Tensor:
+    """y = conv2d(x, weight, bias, stride=1, padding=k // 2, groups=C), k in {3, 5, 7}.
+
+    ``k`` defaults to ``weight.shape[-1]``; ``weight`` is [C,1,k,k] (or any
+    shape with C*k*k elements).  Same layouts and dtypes as depthwise7x7.
+    """
     if not isinstance(x, torch.Tensor) or not x.is_cuda:
         raise ValueError("depthwise7x7 requires a CUDA input")
     if x.dim() != 4:
@@ -42,8 +56,12 @@ def depthwise7x7(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | Non
     N, C, H, W = x.shape
     if not weight.is_cuda or weight.device != x.device:
         raise RuntimeError("weight must be a CUDA tensor on the input's device")
-    if weight.numel() != C * 49 or (weight.dim() == 4 and tuple(weight.shape) != (C, 1, 7, 7)):
-        raise RuntimeError("weight must have shape [C,1,7,7]")
+    if k is None:
+        k = int(weight.shape[-1]) if weight.dim() == 4 else 7
+    if k not in (3, 5, 7):
+        raise RuntimeError("only 3x3, 5x5 and 7x7 filters are supported")
+    if weight.numel() != C * k * k or (weight.dim() == 4 and tuple(weight.shape) != (C, 1, k, k)):
+        raise RuntimeError(f"weight must have shape [C,1,{k},{k}]")
     if weight.dtype != x.dtype:
         raise RuntimeError("dtype mismatch")
     if x.dtype not in _lib.DTYPE_CODE:
@@ -67,26 +85,30 @@ def depthwise7x7(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | Non
     weight = weight.detach().contiguous()
     bias = None if bias is None else bias.detach().contiguous()
     with torch.cuda.device(x.device):
-        st = _lib.lib().pla_depthwise7x7_forward(
-            x.data_ptr(), weight.data_ptr(), _lib.ptr(bias), out.data_ptr(), N, C, H, W,
+        st = _lib.lib().pla_depthwise_forward(
+            x.data_ptr(), weight.data_ptr(), _lib.ptr(bias), out.data_ptr(), N, C, H, W, k,
             _lib.DTYPE_CODE[x.dtype], layout, _lib.stream_ptr(x.device))
-    _lib.check(st, "pla_depthwise7x7_forward")
+    _lib.check(st, "pla_depthwise_forward")
     return out
 
 
 class ModelNew(torch.nn.Module):
-    """KernelBench drop-in for data/depthwise_conv_7x7.py's Model (parameter ``conv2d``)."""
+    """KernelBench drop-in for data/depthwise_conv_7x7.py's Model (parameter ``conv2d``).
+
+    kernel_size 7 with padding 3 is the reference module's case; 3 (padding 1)
+    and 5 (padding 2) cover the MetaSchedule benchmark's other filter size.
+    """
 
     def __init__(self, in_channels: int, kernel_size: int, stride: int = 1, padding: int = 1,
                  bias: bool = False):
         super().__init__()
-        if kernel_size != 7 or stride != 1 or padding != 3:
-            raise ValueError("only kernel_size=7, stride=1, padding=3 is supported")
-        self.conv2d = torch.nn.Conv2d(in_channels, in_channels, 7, stride=1, padding=3,
+        if kernel_size not in (3, 5, 7) or stride != 1 or padding != kernel_size // 2:
+            raise ValueError("only kernel_size 3, 5 or 7 with stride=1 and padding=kernel_size // 2 is supported")
+        self.conv2d = torch.nn.Conv2d(in_channels, in_channels, kernel_size, stride=1, padding=kernel_size // 2,
                                       groups=in_channels, bias=bias)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        return depthwise7x7(x, self.conv2d.weight, self.conv2d.bias)
+        return depthwise_kxk(x, self.conv2d.weight, self.conv2d.bias)
 
 
 # Harness shape of the reference problem (data/depthwise_conv_7x7.py:64-85).

@@ -17,11 +17,21 @@ Low-precision expected values follow the reference tests' convention
 fp32 (fp64 for fp64) on the widened inputs, then cast to the data type.  For
 bf16 the module is also run natively in bf16 and stored as ``y_native``.
 
+The k x k depthwise cases (op "depthwise_ms") come from the reference's
+MetaSchedule benchmark instead: its own numpy check ``ref`` (nested in
+``main`` of benchmark/MetaSchedule/depthwise_conv.py:41-46; fp32 products
+summed in (ry, rx) order, cast to the data type) is lifted out of the source
+with ``ast`` and run on inputs drawn as its harness draws them
+(benchmark/MetaSchedule/common.py:176-177: ``np.random.default_rng(seed)``,
+x then w ~ U(-1, 1), cast to the dtype).  The TVM parts of that file are not
+imported or run.
+
 The fixtures are read at test time; the reference tree is not needed then.
 """
 from __future__ import annotations
 
 import argparse
+import ast
 import importlib.util
 import os
 import sys
@@ -51,6 +61,29 @@ def _nhwc_bits(t: torch.Tensor) -> np.ndarray:
 
 
 DT = {"f32": torch.float32, "bf16": torch.bfloat16, "f16": torch.float16, "f64": torch.float64}
+
+
+def _metaschedule_ref(reference_root):
+    """Factory for the reference's numpy depthwise check, bound to (k, h, w)."""
+    path = os.path.join(reference_root, "benchmark", "MetaSchedule", "depthwise_conv.py")
+    with open(path) as f:
+        tree = ast.parse(f.read())
+    main = next(n for n in tree.body if isinstance(n, ast.FunctionDef) and n.name == "main")
+    fn = next(n for n in ast.walk(main) if isinstance(n, ast.FunctionDef) and n.name == "ref")
+    code = compile(ast.Module(body=[fn], type_ignores=[]), path, "exec")
+
+    def make(k, h, w):
+        ns = {"np": np, "k": k, "pad": k // 2, "h": h, "w": w}  # the names `ref` reads from main's scope
+        exec(code, ns)
+        return ns["ref"]
+
+    return make
+
+
+def _np_to_torch(a: np.ndarray, dtype: str) -> torch.Tensor:
+    if dtype in ("bf16", "f16"):
+        return torch.from_numpy(np.ascontiguousarray(a).view(np.int16).copy()).view(DT[dtype])
+    return torch.from_numpy(np.ascontiguousarray(a))
 
 
 def main(argv=None):
@@ -164,6 +197,28 @@ def main(argv=None):
     dw_case("dw_f64_9x11", (1, 2, 9, 11), 10, "f64")
     dw_case("dw_f16_14", (1, 4, 14, 14), 11, "f16")
     dw_case("dw_f32_nhwc_odd", (2, 35, 9, 10), 12, "f32", "nhwc")
+
+    # ------- k x k depthwise of the MetaSchedule benchmark (its numpy check) -------
+    ms_ref = _metaschedule_ref(args.reference_root)
+
+    def ms_case(name, shape, k, seed, dtype):
+        import ml_dtypes
+
+        npdt = {"f32": np.float32, "f16": np.float16, "bf16": ml_dtypes.bfloat16}[dtype]
+        n, c, h, w = shape
+        rng = np.random.default_rng(seed)
+        x = rng.uniform(-1, 1, (n, c, h, w)).astype(npdt)
+        wt = rng.uniform(-1, 1, (c, 1, k, k)).astype(npdt)
+        y = ms_ref(k, h, w)(x, wt)
+        assert y.dtype == x.dtype
+        record(name, "depthwise_ms", dtype, "nchw", _np_to_torch(x, dtype), _np_to_torch(wt, dtype), None,
+               _np_to_torch(y, dtype))
+
+    ms_case("ms_k3_f32", (1, 8, 64, 64), 3, 0, "f32")
+    ms_case("ms_k3_f16", (1, 8, 64, 64), 3, 1, "f16")
+    ms_case("ms_k3_bf16", (2, 4, 40, 72), 3, 2, "bf16")
+    ms_case("ms_k3_f32_odd", (2, 3, 9, 13), 3, 3, "f32")
+    ms_case("ms_k7_f32", (1, 4, 48, 64), 7, 4, "f32")
 
     # ---------------- iterated stencil (iterated-stencil recipe, reduced) --------
     g = torch.Generator().manual_seed(4)

@@ -10,6 +10,9 @@ import torch
 GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "golden.npz")
 DT = {"f32": torch.float32, "bf16": torch.bfloat16, "f16": torch.float16, "f64": torch.float64}
 TOL = {"f32": 1e-5, "bf16": 2e-2, "f16": 2e-3, "f64": 1e-10}
+# k x k cases of the MetaSchedule benchmark: its own check's tolerance
+# (benchmark/MetaSchedule/common.py:175: 1e-4 for fp32, 1e-2 otherwise).
+MS_TOL = {"f32": 1e-4, "bf16": 1e-2, "f16": 1e-2}
 
 
 @dataclass
@@ -28,7 +31,12 @@ class Case:
 
     @property
     def tol(self) -> float:
-        return TOL[self.dtype]
+        return MS_TOL[self.dtype] if self.op == "depthwise_ms" else TOL[self.dtype]
+
+    @property
+    def k(self) -> int:
+        """Filter side (7 except for the k x k depthwise cases)."""
+        return int(round((self.w.numel() // self.shape[1]) ** 0.5)) if self.op == "depthwise_ms" else 7
 
 
 def _tensor(arr: np.ndarray, dtype: str, shape, layout: str) -> torch.Tensor:

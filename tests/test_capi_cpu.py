@@ -75,10 +75,27 @@ def test_module_interfaces_match_reference():
     assert tuple(m.conv2d.weight.shape) == (8, 1, 7, 7)
     mb = depthwise.ModelNew(16, 7, 1, 3, bias=True)
     assert set(mb.state_dict()) == {"conv2d.weight", "conv2d.bias"}
-    with pytest.raises(ValueError):
-        depthwise.ModelNew(8, 3, 1, 1)
+    # 3x3 with padding 1: the MetaSchedule benchmark's filter
+    # (benchmark/MetaSchedule/depthwise_conv.py:7-13)
+    assert tuple(depthwise.ModelNew(8, 3, 1, 1).conv2d.weight.shape) == (8, 1, 3, 3)
     with pytest.raises(ValueError):
         depthwise.ModelNew(8, 7, 1, 1)  # the reference default padding=1 is not a 7x7 "same" conv
+    with pytest.raises(ValueError):
+        depthwise.ModelNew(8, 3, 1, 0)
+    with pytest.raises(ValueError):
+        depthwise.ModelNew(8, 9, 1, 4)
+
+
+def test_kxk_entry_validates_without_device():
+    from pla_b200 import _lib
+
+    L = _lib.lib()
+    # filter sizes other than 3, 5, 7 and bad layouts are refused before any device work
+    assert L.pla_depthwise_forward(None, None, None, None, 1, 1, 8, 8, 9, 1, 0, None) == 2
+    assert L.pla_depthwise_forward(None, None, None, None, 1, 1, 8, 8, 4, 1, 0, None) == 2
+    assert L.pla_depthwise_forward(None, None, None, None, 1, 1, 8, 8, 3, 1, 7, None) == 1
+    assert L.pla_depthwise_forward(None, None, None, None, 1, 1, 8, 8, 3, 1, 0, None) == 1  # NULL buffers
+    assert L.pla_depthwise_forward(None, None, None, None, 0, 1, 8, 8, 3, 1, 0, None) == 0  # empty
 
 
 def test_halo_and_ipc_argument_validation_needs_no_device():

@@ -57,6 +57,12 @@ def test_golden_cases(case):
         ref = oracle.depthwise7x7(case.x, case.w.reshape(C, 1, 7, 7), case.b)
         if case.layout == "nhwc":
             assert y.is_contiguous(memory_format=torch.channels_last)
+    elif case.op == "depthwise_ms":
+        from pla_b200 import depthwise_kxk
+
+        C, k = case.shape[1], case.k
+        y = depthwise_kxk(x, w.reshape(C, 1, k, k), b)
+        ref = oracle.depthwise(case.x, case.w.reshape(C, 1, k, k), case.b)
     else:
         y = stencil7x7_iterate(x.contiguous(), w, case.steps, b)
         ref = oracle.stencil7x7_iterate(case.x, case.w, case.steps, case.b)
@@ -413,3 +419,55 @@ def test_16bit_paths_with_special_values(dtype, shape, layout):
     x = x.contiguous(memory_format=fmt)
     y = depthwise7x7(x.to(DEV), w.to(DEV), b.to(DEV))
     _assert_equal_nan(y, oracle.depthwise7x7(x, w, b))
+
+
+# --------------------------------------------------------------------------
+# 3x3 / 5x5 depthwise (the MetaSchedule benchmark's operator,
+# benchmark/MetaSchedule/depthwise_conv.py:32-33): every dispatch route
+# (TMA tile kernel for dense NCHW planes, the one-thread-per-output kernel
+# for the rest) bit-identical to the oracle
+# --------------------------------------------------------------------------
+@pytest.mark.parametrize("k", [3, 5])
+@pytest.mark.parametrize("shape,dtype,layout,bias", [
+    ((1, 32, 128, 128), torch.float32, "nchw", False),     # the benchmark's default shape (wide tiles)
+    ((2, 8, 200, 260), torch.float16, "nchw", False),      # wide tiles, ragged edges
+    ((4, 80, 56, 56), torch.bfloat16, "nchw", True),       # narrow 56 x 64 tiles (320 planes)
+    ((1, 4, 40, 40), torch.float32, "nchw", True),         # short tiles (few planes)
+    ((2, 16, 14, 14), torch.bfloat16, "nchw", True),       # small planes: generic kernel
+    ((2, 24, 17, 9), torch.float32, "nhwc", True),         # NHWC: generic kernel
+    ((1, 3, 12, 70), torch.float64, "nchw", True),         # fp64
+])
+def test_depthwise_kxk_matches_oracle(k, shape, dtype, layout, bias):
+    from pla_b200 import depthwise_kxk
+
+    g = torch.Generator().manual_seed(100 + k)
+    N, C, H, W = shape
+    x = (torch.rand(shape, generator=g) * 2 - 1).to(dtype)
+    w = (torch.rand(C, 1, k, k, generator=g) * 2 - 1).to(dtype)
+    b = (torch.rand(C, generator=g) * 0.2 - 0.1).to(dtype) if bias else None
+    if layout == "nhwc":
+        x = x.contiguous(memory_format=torch.channels_last)
+    y = depthwise_kxk(x.to(DEV), w.to(DEV), None if b is None else b.to(DEV))
+    if layout == "nhwc":
+        assert y.is_contiguous(memory_format=torch.channels_last)
+    ref = oracle.depthwise(x, w, b)
+    _assert_equal(y, ref)
+    # and the semantics of torch's grouped conv within the benchmark's tolerance
+    tol = 1e-4 if dtype in (torch.float32, torch.float64) else 1e-2
+    want = torch.nn.functional.conv2d(x.double(), w.double(), None if b is None else b.double(),
+                                      padding=k // 2, groups=C)
+    torch.testing.assert_close(y.cpu().double(), want, rtol=tol, atol=tol)
+
+
+def test_depthwise_kxk_module_and_7x7_route():
+    """ModelNew(C, 3, 1, 1) runs the 3x3 path; k = 7 through the k x k entry is the 7x7 path."""
+    from pla_b200 import depthwise_kxk
+    from pla_b200.depthwise import ModelNew
+
+    m = ModelNew(16, 3, 1, 1).to(DEV)
+    x = torch.randn(2, 16, 64, 64, device=DEV)
+    with torch.no_grad():
+        y = m(x)
+    _assert_equal(y, oracle.depthwise(x.cpu(), m.conv2d.weight.detach().cpu(), None))
+    w7 = torch.randn(16, 1, 7, 7)
+    _assert_equal(depthwise_kxk(x, w7.to(DEV)), oracle.depthwise7x7(x.cpu(), w7))

@@ -20,6 +20,9 @@ def _oracle(case):
     if case.op == "depthwise":
         C = case.shape[1]
         return oracle.depthwise7x7(case.x, case.w.reshape(C, 1, 7, 7), case.b)
+    if case.op == "depthwise_ms":
+        C, k = case.shape[1], case.k
+        return oracle.depthwise(case.x, case.w.reshape(C, 1, k, k), case.b)
     return oracle.stencil7x7_iterate(case.x, case.w, case.steps, case.b)
 
 
