@@ -225,7 +225,9 @@ int launch_tile(const void* x, const void* w, const void* b, const HostTaps* ht,
   a.y_plane_stride = y_plane_stride;
   a.y_row_stride = y_row_stride;
   const long long slots = static_cast<long long>(d->sms) * per_sm;
-  const int grid = static_cast<int>(total < slots ? total : slots);
+  // Long tile lists: one CTA per tile with launch-control claiming (see tile_kernel.cuh).
+  a.dyn = total >= 8 * slots ? 1 : 0;
+  const int grid = static_cast<int>(a.dyn ? total : (total < slots ? total : slots));
   const HaloLinks no_halo{};
   if constexpr (K == 7) {
     if (ht) {
@@ -314,6 +316,7 @@ int launch_tile_halo(const void* in, const HostTaps& ht, void* out_rows, int dty
   st = kernel_setup<tile_kernel<T, kWideR, kWideLX, true, true>>(kTileThreads, G::SMEM, &per_sm);
   if (st != PLA_OK) return st;
   TileArgs a;
+  a.dyn = 0;  // the fused halo step keeps its own edge-first tile order
   a.w = nullptr;
   a.b = nullptr;
   a.y = out_rows;

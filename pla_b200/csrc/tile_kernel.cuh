@@ -5,8 +5,16 @@
 // iterated stencil, whole grid or one row band).
 //
 // Design (sm_100a):
-//  * persistent CTAs (grid = #SMs x resident CTAs) walk a flat list of
-//    TH x TW output tiles, plane-major then row-major;
+//  * CTAs walk a flat list of TH x TW output tiles, plane-major then
+//    row-major.  Short lists: persistent CTAs (grid = #SMs x resident CTAs),
+//    tile t, t + grid, ...  Long lists (>= 8 tiles per resident CTA): one CTA
+//    per tile, and each running CTA takes over the tiles of CTAs not yet
+//    started with Blackwell's cluster launch control
+//    (clusterlaunchcontrol.try_cancel), one claim ahead of its TMA prefetch.
+//    Claimed tiles come in launch order, so the tiles in flight stay a compact
+//    window (DRAM row locality, halo rows still in L2) and SMs finish together:
+//    9 % faster on a 32768^2 band step, 14 % on a 3x3 1x32x1024^2 depthwise;
+//    with fewer tiles per CTA the per-tile claim costs more than it saves;
 //  * each tile's (TH+6) x (TW+2*LEFT) input window is one 3-D TMA tile load
 //    (cp.async.bulk.tensor, no multicast) into a shared-memory ring of NS = 2
 //    stages (3 or 4 stages measured slower for every filter size: the larger
@@ -51,7 +59,8 @@ struct TileGeom {
   static_assert((PITCH * sizeof(T)) % 16 == 0, "TMA box inner extent must be a multiple of 16 B");
   static constexpr uint32_t BYTES = ROWS * PITCH * sizeof(T);
   static constexpr uint32_t STAGE = (BYTES + 127u) & ~127u;
-  static constexpr uint32_t SMEM = NS * STAGE + NS * sizeof(uint64_t);
+  // + NS mbarriers, the launch-control mbarrier, its 16-byte response, 2 tile ids
+  static constexpr uint32_t SMEM = NS * STAGE + 64;
 };
 
 struct TileArgs {
@@ -64,6 +73,7 @@ struct TileArgs {
   int row_begin, row_end;   // output rows computed: [row_begin, row_end)
   int in_row_shift;         // input row (tensor-map y) of output row r is r + in_row_shift
   int tiles_x, tiles_y;     // tiles per plane
+  int dyn;                  // 1: one CTA per tile, pending CTAs' tiles claimed (never with HALO)
   int total_tiles;          // planes * tiles_y * tiles_x (< 2^31, checked on the host)
   FastDiv div_tx, div_ty, div_c;
   long long y_plane_stride; // elements
@@ -117,7 +127,12 @@ __global__ void __launch_bounds__(kTileThreads, HOST_TAPS ? 5 : 4)
   using G = TileGeom<T, R, LX, K>;
   extern __shared__ __align__(128) unsigned char smem[];
   constexpr int NS = G::NS;
+  static_assert(NS == 2, "tile claiming assumes a 2-stage ring");
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + NS * G::STAGE);
+  uint64_t* claim_bar = bars + NS;                                        // byte 16
+  unsigned char* claim_resp = smem + NS * G::STAGE + 32;                  // 16-byte aligned
+  int* next_tile = reinterpret_cast<int*>(smem + NS * G::STAGE + 48);     // [2]
+  const bool dyn = !HALO && a.dyn;
 
   const int tid = threadIdx.x;
   const int lane = tid & 31;
@@ -128,6 +143,7 @@ __global__ void __launch_bounds__(kTileThreads, HOST_TAPS ? 5 : 4)
     prefetch_tensormap(&tmap);
 #pragma unroll
     for (int i = 0; i < NS; ++i) mbar_init(&bars[i], 1);
+    mbar_init(claim_bar, 1);
     fence_mbar_init();
   }
   __syncthreads();
@@ -135,6 +151,15 @@ __global__ void __launch_bounds__(kTileThreads, HOST_TAPS ? 5 : 4)
   const int total = a.total_tiles;
   const int stride = gridDim.x;
   int t = blockIdx.x;
+  bool claiming = dyn;
+  // Thread 0: ask for the tile of a CTA that has not started yet; the
+  // response (16 bytes) lands in claim_resp and completes claim_bar.
+  auto claim = [&]() {
+    mbar_arrive_expect_tx(claim_bar, 16);
+    asm volatile("clusterlaunchcontrol.try_cancel.async.shared::cta.mbarrier::complete_tx::bytes.b128 [%0], [%1];"
+                 ::"r"(smem_u32(claim_resp)), "r"(smem_u32(claim_bar))
+                 : "memory");
+  };
 
   auto issue = [&](int tile, int stage) {
     const int q = fdiv(tile, a.div_tx);
@@ -159,7 +184,8 @@ __global__ void __launch_bounds__(kTileThreads, HOST_TAPS ? 5 : 4)
   if (tid == 0) {
 #pragma unroll
     for (int j = 0; j < NS - 1; ++j)
-      if (t + j * stride < total) issue(t + j * stride, j);
+      if (dyn ? j == 0 : t + j * stride < total) issue(t + j * stride, j);
+    if (dyn) claim();
   }
 
   const T* wt_base = static_cast<const T*>(a.w);
@@ -171,11 +197,40 @@ __global__ void __launch_bounds__(kTileThreads, HOST_TAPS ? 5 : 4)
   int cur_c = -1;
   float bias = 0.f;
 
-  for (int it = 0; t < total; ++it, t += stride) {
+  for (int it = 0; t < total; ++it) {
     const int stage = it % NS;
-    // Tile it + NS - 1 goes into the stage that tile it - 1 used; every
-    // thread left that stage at the barrier that ended iteration it - 1.
-    if (tid == 0 && t + (NS - 1) * stride < total) issue(t + (NS - 1) * stride, (it + NS - 1) % NS);
+    if (dyn) {
+      // The claim made one tile ago: on success prefetch that tile into the
+      // other stage and claim again; a failed claim (or a wait past its
+      // bound) ends this CTA after the current tile.  No claim follows a
+      // failed one.
+      if (tid == 0) {
+        int nt = -1;
+        if (claiming && mbar_wait_bounded(claim_bar, it & 1)) {
+          int ok = 0;
+          asm volatile(
+              "{ .reg .b128 r; .reg .pred p; ld.shared.b128 r, [%2];\n"
+              " clusterlaunchcontrol.query_cancel.is_canceled.pred.b128 p, r;\n"
+              " selp.s32 %0, 1, 0, p;\n"
+              " @p clusterlaunchcontrol.query_cancel.get_first_ctaid::x.b32.b128 %1, r; }"
+              : "=r"(ok), "+r"(nt)
+              : "r"(smem_u32(claim_resp))
+              : "memory");
+          if (!ok) nt = -1;
+        }
+        if (nt >= 0) {
+          issue(nt, stage ^ 1);
+          claim();
+        } else {
+          claiming = false;
+        }
+        next_tile[it & 1] = nt;  // read by every thread after this iteration's barrier
+      }
+    } else if (tid == 0 && t + (NS - 1) * stride < total) {
+      // Tile it + NS - 1 goes into the stage that tile it - 1 used; every
+      // thread left that stage at the barrier that ended iteration it - 1.
+      issue(t + (NS - 1) * stride, (it + NS - 1) % NS);
+    }
 
     const int q = fdiv(t, a.div_tx);
     const int tx = t - q * a.tiles_x;
@@ -310,6 +365,12 @@ __global__ void __launch_bounds__(kTileThreads, HOST_TAPS ? 5 : 4)
           }
         }
       }
+    }
+    if (dyn) {
+      t = next_tile[it & 1];
+      if (t < 0) break;
+    } else {
+      t += stride;
     }
   }
 }
