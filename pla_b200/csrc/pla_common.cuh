@@ -208,7 +208,9 @@ __device__ __forceinline__ bool wait_flag_geq(const unsigned int* flag, unsigned
       if (ld_acquire_sys(flag) >= target) return true;
       __nanosleep(128);
     }
-    if (global_timer_ns() - t0 > limit_ns) {
+    // Past the bound, or another wait already gave up (the neighbour is not
+    // answering): record and stop, so later edge tiles do not wait again.
+    if (global_timer_ns() - t0 > limit_ns || (*reinterpret_cast<volatile unsigned int*>(&g_device_faults) & 2u)) {
       atomicOr(&g_device_faults, 2u);
       return false;
     }

@@ -73,7 +73,7 @@ struct TileArgs {
   int row_begin, row_end;   // output rows computed: [row_begin, row_end)
   int in_row_shift;         // input row (tensor-map y) of output row r is r + in_row_shift
   int tiles_x, tiles_y;     // tiles per plane
-  int dyn;                  // 1: one CTA per tile, pending CTAs' tiles claimed (never with HALO)
+  int dyn;                  // 1: one CTA per tile, pending CTAs' tiles claimed
   int total_tiles;          // planes * tiles_y * tiles_x (< 2^31, checked on the host)
   FastDiv div_tx, div_ty, div_c;
   long long y_plane_stride; // elements
