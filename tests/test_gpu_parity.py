@@ -471,3 +471,31 @@ def test_depthwise_kxk_module_and_7x7_route():
     _assert_equal(y, oracle.depthwise(x.cpu(), m.conv2d.weight.detach().cpu(), None))
     w7 = torch.randn(16, 1, 7, 7)
     _assert_equal(depthwise_kxk(x, w7.to(DEV)), oracle.depthwise7x7(x.cpu(), w7))
+
+
+@pytest.mark.parametrize("k,dtype", [(7, torch.float32), (3, torch.float32), (7, torch.bfloat16)])
+def test_tile_claiming_path(k, dtype):
+    """8 planes of 2048^2 make 8192 tiles of 32 x 128, more than 8 per resident
+    CTA: the tile kernel launches one CTA per tile and the running CTAs claim
+    the rest (cluster launch control).  Every tile must be computed exactly once."""
+    from pla_b200 import depthwise_kxk
+
+    g = torch.Generator().manual_seed(300 + k)
+    x = torch.randn(1, 8, 2048, 2048, generator=g).to(dtype)
+    w = (torch.randn(8, 1, k, k, generator=g) / k).to(dtype)
+    b = (torch.randn(8, generator=g) * 0.1).to(dtype)
+    y = torch.full_like(x, float("nan"), device=DEV)  # a tile left out stays NaN
+    depthwise_kxk(x.to(DEV), w.to(DEV), b.to(DEV), out=y)
+    assert not torch.isnan(y).any()
+    _assert_equal(y, oracle.depthwise(x, w, b))
+    assert _lib_faults() == 0
+
+
+def _lib_faults() -> int:
+    import ctypes
+
+    from pla_b200 import _lib
+
+    v = ctypes.c_uint(0)
+    _lib.check(_lib.lib().pla_read_device_faults(ctypes.byref(v)), "pla_read_device_faults")
+    return v.value
