@@ -73,7 +73,7 @@ PLA_API const char* pla_status_string(int status);
  * (CUDA error strings, size limits). */
 PLA_API const char* pla_last_cuda_error(void);
 
-/* Library ABI version: (major << 16) | minor. */
+/* Library ABI version: (major << 16) | minor.  1.1 added pla_depthwise_forward. */
 PLA_API int pla_version(void);
 
 /*

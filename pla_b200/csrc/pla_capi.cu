@@ -689,7 +689,7 @@ const char* pla_status_string(int status) {
 
 const char* pla_last_cuda_error(void) { return g_last_cuda_error; }
 
-int pla_version(void) { return (1 << 16) | 0; }
+int pla_version(void) { return (1 << 16) | 1; }  // 1.1: pla_depthwise_forward (k x k)
 
 int pla_stencil7x7_forward(const void* x, const void* w, const void* b, void* y, int n, int h, int width,
                            int64_t sn, int64_t sh, int64_t sw, int dtype, pla_stream_t stream) {
