@@ -3,8 +3,9 @@
  * with gcc against include/pla_b200.h and pla_b200/libpla_b200.so.
  *
  *   abi_example cpu   status strings, version, argument checks (no device)
- *   abi_example gpu   cudaMalloc'd buffers, one stencil step on the current
- *                     device, result checked against a scalar C loop
+ *   abi_example gpu   cudaMalloc'd buffers, one stencil step and one 3x3
+ *                     depthwise call on the current device, results checked
+ *                     against scalar C loops
  */
 #include <math.h>
 #include <stdio.h>
@@ -28,6 +29,9 @@ static int check_cpu(void) {
       PLA_ERR_INVALID_ARGUMENT)
     return 4;
   if (pla_stencil7x7_forward(NULL, NULL, NULL, NULL, 0, 8, 8, 64, 8, 1, PLA_F32, NULL) != PLA_OK) return 5;
+  if ((pla_version() & 0xffff) < 1) return 6; /* 1.1: pla_depthwise_forward */
+  if (pla_depthwise_forward(NULL, NULL, NULL, NULL, 1, 1, 8, 8, 4, PLA_F32, PLA_NCHW, NULL) != PLA_ERR_UNSUPPORTED)
+    return 7;
   printf("cpu ok\n");
   return 0;
 }
@@ -66,6 +70,28 @@ static int check_gpu(void) {
       if (acc != hy[i * W + j]) {
         fprintf(stderr, "mismatch at %d,%d: %.9g vs %.9g\n", i, j, acc, hy[i * W + j]);
         return 12;
+      }
+    }
+  /* 3x3 depthwise, one channel, no bias: the first 9 taps as the filter */
+  st = pla_depthwise_forward(dx, dw, NULL, dy, 1, 1, H, W, 3, PLA_F32, PLA_NCHW, NULL);
+  if (st != PLA_OK) {
+    fprintf(stderr, "pla_depthwise_forward: %s %s\n", pla_status_string(st), pla_last_cuda_error());
+    return 13;
+  }
+  cudaDeviceSynchronize();
+  cudaMemcpy(hy, dy, n * 4, 2);
+  for (int i = 0; i < H; ++i)
+    for (int j = 0; j < W; ++j) {
+      float acc = 0.0f;
+      for (int ky = 0; ky < 3; ++ky)
+        for (int kx = 0; kx < 3; ++kx) {
+          const int r = i + ky - 1, c = j + kx - 1;
+          if (r < 0 || r >= H || c < 0 || c >= W) continue;
+          acc = fmaf(hx[r * W + c], hw[ky * 3 + kx], acc);
+        }
+      if (acc != hy[i * W + j]) {
+        fprintf(stderr, "3x3 mismatch at %d,%d: %.9g vs %.9g\n", i, j, acc, hy[i * W + j]);
+        return 14;
       }
     }
   cudaFree(dx);
