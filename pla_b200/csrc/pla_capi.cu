@@ -13,6 +13,7 @@
 #include "../../include/pla_b200.h"
 #include "cm_kernel.cuh"
 #include "generic_kernel.cuh"
+#include "nhwc_tile_kernel.cuh"
 #include "pla_common.cuh"
 #include "stack_kernel.cuh"
 #include "tile_kernel.cuh"
@@ -529,6 +530,63 @@ int launch_stack(const void* x, const void* w, const void* b, void* y, int dtype
 
 // Square planes of side 7, 14 or 28 (and, for NHWC, channel rows that are
 // 16-byte multiples so the 4-D TMA map is legal).
+// NHWC planes the stack kernel does not take: 14 x 14 spatial tiles x 32
+// channels (nhwc_tile_kernel.cuh).  TMA needs 16-byte aligned bases and a
+// channel stride (C * element size) that is a multiple of 16 bytes.
+bool nhwc_tile_ok(const void* x, const void* y, int dtype, long long n, long long c, int h, int w) {
+  if (dtype != PLA_F32 && dtype != PLA_BF16 && dtype != PLA_F16) return false;
+  if (!aligned(x, 16) || !aligned(y, 16)) return false;
+  if ((c * static_cast<long long>(dtype_size(dtype))) % 16 != 0) return false;
+  const long long tiles = static_cast<long long>((h + 13) / 14) * ((w + 13) / 14);
+  return n * tiles * ((c + 31) / 32) < 0x7fffffffll;
+}
+
+template <typename T>
+int launch_nhwc_tile(const void* x, const void* w, const void* b, void* y, int dtype, int n, int c, int h,
+                     int width, cudaStream_t stream) {
+  using G = NhwcTileGeom;
+  using M = NhwcTileSmem<T>;
+  int st;
+  DeviceInfo* d = device_info(&st);
+  if (!d) return st;
+  CUtensorMap xmap, ymap;
+  st = make_nhwc_map<T>(&xmap, x, dtype, n, c, h, width, G::LANES, G::SW);
+  if (st != PLA_OK) return st;
+  st = make_nhwc_map<T>(&ymap, y, dtype, n, c, h, width, G::LANES, G::TS);
+  if (st != PLA_OK) return st;
+  NhwcTileArgs a;
+  a.w = w;
+  a.b = b;
+  a.N = n;
+  a.C = c;
+  a.cgroups = (c + G::LANES - 1) / G::LANES;
+  a.tiles_x = (width + G::TS - 1) / G::TS;
+  a.tiles_y = (h + G::TS - 1) / G::TS;
+  a.tiles = a.tiles_x * a.tiles_y;
+  a.stages = a.cgroups * n * a.tiles;
+  a.div_stage_cg = make_fastdiv(n * a.tiles);
+  a.div_tiles = make_fastdiv(a.tiles);
+  a.div_tx = make_fastdiv(a.tiles_x);
+  int per_sm;
+  st = kernel_setup<nhwc_tile_kernel<T>>(G::THREADS, M::TOTAL, &per_sm);
+  if (st != PLA_OK) return st;
+  const long long slots = static_cast<long long>(d->sms) * per_sm;
+  const int grid = static_cast<int>(a.stages < slots ? a.stages : slots);
+  nhwc_tile_kernel<T><<<grid, G::THREADS, M::TOTAL, stream>>>(xmap, ymap, a);
+  PLA_CUDA(cudaGetLastError());
+  return PLA_OK;
+}
+
+int launch_nhwc_tile_dtype(int dtype, const void* x, const void* w, const void* b, void* y, int n, int c, int h,
+                           int width, cudaStream_t stream) {
+  switch (dtype) {
+    case PLA_F32: return launch_nhwc_tile<float>(x, w, b, y, dtype, n, c, h, width, stream);
+    case PLA_BF16: return launch_nhwc_tile<__nv_bfloat16>(x, w, b, y, dtype, n, c, h, width, stream);
+    case PLA_F16: return launch_nhwc_tile<__half>(x, w, b, y, dtype, n, c, h, width, stream);
+    default: return PLA_ERR_UNSUPPORTED;
+  }
+}
+
 bool stack_path_ok(const void* x, const void* y, int dtype, int layout, long long n, long long c, int h, int w) {
   if (dtype != PLA_F32 && dtype != PLA_BF16 && dtype != PLA_F16) return false;
   if (h != w || (h != 7 && h != 14 && h != 28)) return false;
@@ -722,6 +780,8 @@ int pla_depthwise7x7_forward(const void* x, const void* w, const void* b, void* 
       return launch_tile_dtype(dtype, x, w, b, nullptr, y, static_cast<int>(planes), c, h, width, width, plane, 0,
                                h, 0, plane, width, s);
     }
+    if (layout == PLA_NHWC && nhwc_tile_ok(x, y, dtype, n, c, h, width))
+      return launch_nhwc_tile_dtype(dtype, x, w, b, y, n, c, h, width, s);
     CmArgs a;
     a.x = x; a.w = w; a.b = b; a.y = y;
     a.N = n; a.C = c; a.H = h; a.W = width;

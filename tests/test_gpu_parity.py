@@ -499,3 +499,22 @@ def _lib_faults() -> int:
     v = ctypes.c_uint(0)
     _lib.check(_lib.lib().pla_read_device_faults(ctypes.byref(v)), "pla_read_device_faults")
     return v.value
+
+
+@pytest.mark.parametrize("shape,dtype,bias", [
+    ((2, 96, 56, 56), torch.bfloat16, False),   # ConvNeXt stage-1 planes in channels_last
+    ((1, 40, 33, 45), torch.float32, True),     # ragged tiles, last channel group partial
+    ((2, 64, 20, 9), torch.float16, True),
+    ((3, 8, 3, 5), torch.bfloat16, True),       # planes smaller than one tile
+    ((1, 32, 100, 30), torch.float32, False),
+])
+def test_nhwc_spatial_tiles_match_oracle(shape, dtype, bias):
+    """channels_last planes outside the plane-stack sizes run 14 x 14 spatial
+    tiles of 32 channels (TMA zero fill at the image edge, clipped TMA stores)."""
+    from pla_b200 import depthwise7x7
+
+    x, w, b = _dw_inputs(400 + shape[1], shape, dtype, bias)
+    x = x.contiguous(memory_format=torch.channels_last)
+    y = depthwise7x7(x.to(DEV), w.to(DEV), None if b is None else b.to(DEV))
+    assert y.is_contiguous(memory_format=torch.channels_last)
+    _assert_equal(y, oracle.depthwise7x7(x, w, b))
