@@ -20,6 +20,9 @@ one JSON line.  Workloads (the benchmark configurations; synthetic seeded inputs
   dw_k3          3x3 depthwise fp32 1x32x1024x1024, no bias: the operator and
                  input recipe of the reference's MetaSchedule benchmark
                  (benchmark/MetaSchedule/depthwise_conv.py, common.py)
+  dwln_cfg4      the dw_cfg4 stages in channels_last with the next ConvNeXt
+                 layer, LayerNorm over C, fused into the depthwise launch
+                 (no reference counterpart; the unfused pair is timed beside it)
 
 A "step" is one pass of the hot path over one batch of input already resident
 in HBM; consecutive steps rotate over enough buffer sets that every step's
@@ -516,6 +519,116 @@ class DwCfg4(DepthwiseBase):
         return slice(a, a + base + (1 if rank < extra else 0))
 
 
+class DwLnCfg4(DwCfg4):
+    """dw_cfg4's ConvNeXt-T stages (seed 3) in channels_last, each followed by
+    LayerNorm over C fused into the same launch (pla_depthwise7x7_layernorm_nhwc).
+
+    LayerNorm scale / shift: 1 + 0.1 N(0,1) and 0.1 N(0,1) from a second
+    generator seeded 3.  Compulsory bytes add the scale and shift.
+    """
+
+    name = "depthwise7x7_layernorm_cfg4_convnext_t_N256_bf16_nhwc"
+    layout = "nhwc"
+    ln_params = 2  # scale and shift: C elements each
+
+    def __init__(self, rank, world, dev):
+        super().__init__(rank, world, dev)
+        from pla_b200.depthwise import depthwise7x7_layernorm
+
+        g = torch.Generator().manual_seed(3)
+        es = torch.tensor([], dtype=self.torch_dtype).element_size()
+        self.norm = []
+        for (x, _, _) in self.items:
+            C = x.shape[1]
+            gamma = (1 + 0.1 * torch.randn(C, generator=g)).to(self.torch_dtype)
+            beta = (0.1 * torch.randn(C, generator=g)).to(self.torch_dtype)
+            self.norm.append((gamma, beta))
+            self.bytes += 2 * C * es
+        self._fn = None
+        if dev is None:
+            return
+        from pla_b200 import _lib
+
+        self.dev_norm = [(g_.to(dev), b_.to(dev)) for (g_, b_) in self.norm]
+        self._ln_fn = depthwise7x7_layernorm
+        self._call = _lib.lib().pla_depthwise7x7_layernorm_nhwc
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        code = _lib.DTYPE_CODE[self.torch_dtype]
+        self._args = []
+        for k in range(self.nsets):
+            per = []
+            for (xs, ys, w, b), (gd, bd) in zip(self.dev_items, self.dev_norm):
+                N, C, H, W = xs[k].shape
+                per.append((xs[k].data_ptr(), w.data_ptr(), None if b is None else b.data_ptr(), gd.data_ptr(),
+                            bd.data_ptr(), 1e-6, ys[k].data_ptr(), N, C, H, W, code, stream))
+            self._args.append(per)
+
+    def config(self):
+        c = super().config()
+        c.update({"layernorm": "over C per pixel, eps 1e-6, scale 1+0.1N(0,1), shift 0.1N(0,1), fp32 math on "
+                               "the bf16-rounded depthwise outputs"})
+        return c
+
+    def e2e_step(self, i, s_in, s_cmp, s_out, ev):
+        self._fn = lambda d, w, b: self._ln_fn(d, w, b, *self.dev_norm[self._stage_of_input(d)], eps=1e-6)
+        return super().e2e_step(i, s_in, s_cmp, s_out, ev)
+
+    def _stage_of_input(self, d):
+        return [xs[0].shape for (xs, _, _, _) in self.dev_items].index(d.shape)
+
+    def unfused_ms(self, steps):
+        """Device time per step of the unfused pair on the same inputs: this
+        library's NHWC depthwise, then torch's LayerNorm on the NHWC view."""
+        from pla_b200.depthwise import depthwise7x7
+
+        def one(i):
+            k = i % self.nsets
+            for (xs, ys, w, b), (gd, bd) in zip(self.dev_items, self.dev_norm):
+                y = depthwise7x7(xs[k], w, b, out=ys[k])
+                torch.nn.functional.layer_norm(y.permute(0, 2, 3, 1), (y.shape[1],), gd, bd, 1e-6)
+
+        for i in range(3):
+            one(i)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record()
+        for i in range(steps):
+            one(i)
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / steps
+
+    def cpu_reference(self):
+        from oracle.reference_modules import DepthwiseModel
+
+        mods = []
+        for (x, w, b), (gamma, beta) in zip(self.items, self.norm):
+            C = x.shape[1]
+            m = DepthwiseModel(C, 7, 1, 3, bias=b is not None).to(self.torch_dtype)
+            with torch.no_grad():
+                m.conv2d.weight.copy_(w)
+            mods.append((m, x.contiguous(memory_format=torch.channels_last), gamma, beta))
+        nb = self.items[0][0].shape[0]
+        es = torch.tensor([], dtype=self.torch_dtype).element_size()
+
+        def run_rows(r0, r1):
+            with torch.no_grad():
+                for m, xx, gamma, beta in mods:
+                    y = m(xx[r0:r1])
+                    torch.nn.functional.layer_norm(y.permute(0, 2, 3, 1), (y.shape[1],), gamma, beta, 1e-6)
+
+        def bytes_rows(nimg):
+            tot = 0
+            for (x, w, b) in self.items:
+                _, C, H, W = x.shape
+                pts = nimg * C * H * W
+                tot += compulsory_bytes(pts, pts, es, C * TAPS, 2 * C, es)
+            return tot
+
+        return run_rows, bytes_rows, nb, "torch.nn.Conv2d(C,C,7,padding=3,groups=C) (data/depthwise_conv_7x7.py " \
+                                         "Model) then torch.nn.functional.layer_norm over C, CPU, channels_last"
+
+
 class IterateCfg5:
     """one Jacobi step of the 32768^2 fp32 grid, row-band partitioned."""
 
@@ -606,7 +719,8 @@ class IterateCfg5:
 
 
 WORKLOADS = {"stencil_cfg2": StencilCfg2, "dw_cfg1": DwCfg1, "dw_cfg3_nchw": DwCfg3Nchw,
-             "dw_cfg3_nhwc": DwCfg3Nhwc, "dw_cfg4": DwCfg4, "iterate_cfg5": IterateCfg5, "dw_k3": DwK3}
+             "dw_cfg3_nhwc": DwCfg3Nhwc, "dw_cfg4": DwCfg4, "iterate_cfg5": IterateCfg5, "dw_k3": DwK3,
+             "dwln_cfg4": DwLnCfg4}
 
 
 # ---------------------------------------------------------------------------
@@ -777,13 +891,20 @@ def main():
         dx = wl.items[d][0]
         es = dx.element_size()
         kernel_bytes = compulsory_bytes(dx.numel(), dx.numel(), es, dx.shape[1] * TAPS,
-                                        dx.shape[1] if wl.items[d][2] is not None else 0, es)
+                                        dx.shape[1] * ((wl.items[d][2] is not None) + getattr(wl, "ln_params", 0)),
+                                        es)
         kernel_ms = dom_ms
         kernel_what = f"launch of stage {list(dx.shape)} (the step's largest), CUDA events in the timed region"
     sm_mhz = clocks.get("sm_mhz") or 1965
     fma_gpts = torch.cuda.get_device_properties(dev).multi_processor_count * FMA_PER_SM_PER_CLK * sm_mhz * 1e6 \
         / getattr(wl, "taps", TAPS) / 1e9
 
+    unfused = None
+    if hasattr(wl, "unfused_ms"):
+        u_ms = wl.unfused_ms(max(3, min(K, 50)))
+        unfused = {"ms_per_step": u_ms, "value": wl.bytes / (u_ms * 1e-3) / 1e9, "unit": "GB/s",
+                   "what": "same inputs, unfused: pla_b200 NHWC depthwise, then torch.nn.functional.layer_norm "
+                           "on the NHWC view (a second pass over HBM)"}
     traffic, traffic_src = profiled_traffic(wl.name)
     cpu_baseline = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -807,7 +928,7 @@ def main():
                          "step_achieved": achieved, "step_frac": achieved / peak,
                          "fma_ceiling_gpoints_per_s": fma_gpts,
                          "fma_frac": (job_points / world) / (mean_step_ms * 1e-3) / 1e9 / fma_gpts},
-            "cpu_baseline": cpu_baseline, "e2e": e2e,
+            "cpu_baseline": cpu_baseline, "e2e": e2e, **({"unfused_pair": unfused} if unfused else {}),
             "gpu_launches": K * wl.launches_per_step, "clocks": clocks,
             "wall_s_timed_region": t_wall,
         }

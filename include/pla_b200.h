@@ -73,7 +73,8 @@ PLA_API const char* pla_status_string(int status);
  * (CUDA error strings, size limits). */
 PLA_API const char* pla_last_cuda_error(void);
 
-/* Library ABI version: (major << 16) | minor.  1.1 added pla_depthwise_forward. */
+/* Library ABI version: (major << 16) | minor.  1.1 added pla_depthwise_forward,
+ * 1.2 pla_depthwise7x7_layernorm_nhwc. */
 PLA_API int pla_version(void);
 
 /*
@@ -142,6 +143,32 @@ PLA_API int pla_depthwise7x7_forward(const void* x, const void* w, const void* b
 PLA_API int pla_depthwise_forward(const void* x, const void* w, const void* b, void* y,
                                   int n, int c, int h, int width, int k,
                                   int dtype, int layout, pla_stream_t stream);
+
+/*
+ * Depthwise 7x7 followed by LayerNorm over the channels of every pixel, in
+ * one pass over HBM: the "dwconv -> norm" pair of a ConvNeXt block,
+ *     v = depthwise7x7(x; w, b) rounded to dtype   (pla_depthwise7x7_forward)
+ *     y[n,i,j,:] = (v[n,i,j,:] - mean) / sqrt(var + eps) * gamma + beta
+ * with mean / biased variance over the C channels of the pixel.
+ *
+ * No reference counterpart: the reference's operator is the depthwise half
+ * (data/depthwise_conv_7x7.py:15-29, whose CUDA launchers
+ * pla_depthwise7x7_forward replaces); the LayerNorm is the next layer of the
+ * ConvNeXt stages its benchmark shapes come from.
+ *
+ * x and y are channels_last (NHWC) [n, h, width, c], dense, of dtype f32 /
+ * bf16 / f16, and must not overlap; w [c,1,7,7]; b, gamma, beta [c] of the
+ * same dtype or NULL (no bias / scale 1 / shift 0); eps >= 0.  The
+ * normalisation runs in fp32 on the rounded depthwise outputs in a fixed
+ * order (sums per 32-channel group, then over the groups), one rounding of
+ * y.  Supported: c * element size a multiple of 16 bytes and at most 16
+ * channel groups per pixel (c <= 512; c <= 2048 for 7 x 7 planes, whose
+ * groups hold 128 channels); other shapes return PLA_ERR_UNSUPPORTED.
+ */
+PLA_API int pla_depthwise7x7_layernorm_nhwc(const void* x, const void* w, const void* b,
+                                            const void* gamma, const void* beta, float eps,
+                                            void* y, int n, int c, int h, int width, int dtype,
+                                            pla_stream_t stream);
 
 /*
  * Iterated stencil on one device (no reference counterpart; the reference

@@ -57,6 +57,9 @@ def _load():
         lib.oracle_depthwise.restype = i32
         lib.oracle_depthwise_f64.argtypes = [vp, vp, vp, vp, i32, i32, i32, i32, i32, i32]
         lib.oracle_depthwise_f64.restype = i32
+        lib.oracle_depthwise7x7_layernorm_nhwc.argtypes = [vp, vp, vp, vp, vp, ctypes.c_float, vp, i32, i32, i32,
+                                                           i32, i32, i32, i32]
+        lib.oracle_depthwise7x7_layernorm_nhwc.restype = i32
         _lib = lib
     return _lib
 
@@ -171,3 +174,40 @@ def stencil7x7_iterate(x: torch.Tensor, w: torch.Tensor, steps: int, b: torch.Te
     for _ in range(steps):
         u = depthwise7x7(u, w.reshape(1, 49), None if b is None else b.reshape(1), threads)
     return u.view(H, W)
+
+
+def depthwise7x7_layernorm(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None, gamma: torch.Tensor | None,
+                           beta: torch.Tensor | None, eps: float = 1e-6, threads: int | None = None) -> torch.Tensor:
+    """Oracle of depthwise 7x7 followed by LayerNorm over channels (NHWC).
+
+    ``x`` is a CPU tensor [N, C, H, W] (any memory format; computed in
+    channels_last), ``w`` [C, 1, 7, 7], ``b``/``gamma``/``beta`` [C] or None,
+    all of x's dtype (fp32 / bf16 / fp16).  Returns a channels_last tensor.
+    The evaluation order is the one documented in pla_oracle.c.
+    """
+    lib = _load()
+    assert x.device.type == "cpu" and x.dim() == 4 and x.dtype != torch.float64
+    x = x.contiguous(memory_format=torch.channels_last)
+    N, C, H, W = x.shape
+    w = w.detach().reshape(C, 49).to(x.dtype).contiguous()
+    vecs = [None if t is None else t.detach().reshape(C).to(x.dtype).contiguous() for t in (b, gamma, beta)]
+    ptrs = [None if t is None else t.data_ptr() for t in vecs]
+    y = torch.zeros_like(x)
+    if x.numel() == 0:
+        return y
+    code = _DTYPE_CODE[x.dtype]
+    nthr = min(threads or default_threads(), N)
+
+    def run(job):
+        return lib.oracle_depthwise7x7_layernorm_nhwc(x.data_ptr(), w.data_ptr(), ptrs[0], ptrs[1], ptrs[2],
+                                                      float(eps), y.data_ptr(), N, C, H, W, code, job[0], job[1])
+
+    step = max(1, -(-N // nthr))
+    jobs = [(n0, min(N, n0 + step)) for n0 in range(0, N, step)]
+    if len(jobs) == 1:
+        rc = run(jobs[0])
+        assert rc == 0, rc
+    else:
+        with ThreadPoolExecutor(nthr) as ex:
+            assert all(rc == 0 for rc in ex.map(run, jobs))
+    return y

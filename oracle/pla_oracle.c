@@ -228,3 +228,64 @@ int oracle_stencil7x7_iterate_f32(const float* x, const float* w, const float* b
   if (src != y) memcpy(y, src, (size_t)plane * sizeof(float));
   return 0;
 }
+
+/*
+ * Depthwise 7x7 followed by LayerNorm over the channels of every pixel, on
+ * channels_last (NHWC) data: the "dwconv -> norm" pair of a ConvNeXt block
+ * (nn.Conv2d(C, C, 7, padding=3, groups=C) then nn.LayerNorm(C, eps) on the
+ * channels-last view).  The reference has no counterpart; its depthwise
+ * operator (data/depthwise_conv_7x7.py:15-29) is the first half, and the
+ * LayerNorm restates torch.nn.LayerNorm's published definition
+ * (biased variance, eps inside the square root).
+ *
+ * Images [n0, n1).  The depthwise output is exactly oracle_depthwise's (one
+ * rounding to dtype); the normalisation then reads those rounded values v_c
+ * (widened to fp32) and evaluates, per pixel, in this fixed order:
+ *   S    = sum over 32-channel groups g = 0, 1, ... of P_g, where
+ *          P_g = sum of v_c over the group's channels in ascending order,
+ *          both sums starting from +0 (separate adds, no fusion)
+ *   mean = S / C
+ *   M    = the same grouping over d_c * d_c, d_c = v_c - mean
+ *   inv  = 1 / sqrt(M / C + eps)
+ *   z_c  = ((d_c * inv) * gamma_c) + beta_c   (gamma / beta skipped if NULL)
+ * every operation correctly rounded fp32, then one rounding of z_c to dtype.
+ * The CUDA epilogue evaluates the same expression tree.
+ */
+int oracle_depthwise7x7_layernorm_nhwc(const void* x, const void* w, const void* b, const void* gamma,
+                                       const void* beta, float eps, void* y, int N, int C, int H, int W,
+                                       int dtype, int n0, int n1) {
+  if (dtype == ORACLE_F64) return -1;
+  if (n0 < 0) n0 = 0;
+  if (n1 > N) n1 = N;
+  if (n0 >= n1 || C <= 0) return 0;
+  int rc = oracle_depthwise(x, w, b, y, N, C, H, W, 7, dtype, ORACLE_NHWC, (int64_t)n0 * C, (int64_t)n1 * C, 0, H);
+  if (rc != 0) return rc;
+  const float fc = (float)C;
+  for (int64_t px = (int64_t)n0 * H * W; px < (int64_t)n1 * H * W; ++px) {
+    const int64_t base = px * C;
+    float s = 0.0f;
+    for (int g = 0; g < C; g += 32) {
+      float part = 0.0f;
+      for (int c = g; c < C && c < g + 32; ++c) part = part + load_f(y, base + c, dtype);
+      s = s + part;
+    }
+    const float mean = s / fc;
+    float m = 0.0f;
+    for (int g = 0; g < C; g += 32) {
+      float part = 0.0f;
+      for (int c = g; c < C && c < g + 32; ++c) {
+        const float d = load_f(y, base + c, dtype) - mean;
+        part = part + d * d;
+      }
+      m = m + part;
+    }
+    const float inv = 1.0f / sqrtf(m / fc + eps);
+    for (int c = 0; c < C; ++c) {
+      float t = (load_f(y, base + c, dtype) - mean) * inv;
+      if (gamma) t = t * load_f(gamma, c, dtype);
+      if (beta) t = t + load_f(beta, c, dtype);
+      store_f(y, base + c, t, dtype);
+    }
+  }
+  return 0;
+}

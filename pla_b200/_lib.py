@@ -36,6 +36,8 @@ SIGNATURES = {
     "pla_stencil7x7_forward_taps": ([_vp, _f32p, _f32p, _vp, _i32, _i32, _i32, _i64, _i64, _i64, _i32, _vp], _i32),
     "pla_depthwise7x7_forward": ([_vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _i32, _vp], _i32),
     "pla_depthwise_forward": ([_vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _vp], _i32),
+    "pla_depthwise7x7_layernorm_nhwc": ([_vp, _vp, _vp, _vp, _vp, ctypes.c_float, _vp, _i32, _i32, _i32, _i32, _i32,
+                                         _vp], _i32),
     "pla_stencil7x7_iterate": ([_vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _vp], _i32),
     "pla_stencil7x7_iterate_noalloc": ([_vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _vp], _i32),
     "pla_stencil7x7_iterate_taps": ([_vp, _f32p, _f32p, _vp, _vp, _i32, _i32, _i32, _i32, _vp], _i32),

@@ -19,8 +19,14 @@
 // 49 taps in registers.  Same tap order and rounding as every kernel here.
 // CTAs own contiguous runs of stages ordered channel-group-major, so a CTA
 // reloads its filters only when its channel group changes.
+//
+// LN: the stage's outputs go through the channel LayerNorm epilogue of
+// ln_epilogue.cuh before the store; the kernel then runs as clusters of
+// ceil(C / 32) CTAs, rank r taking channel group r of the (image, tile)
+// stages its cluster visits.
 #pragma once
 
+#include "ln_epilogue.cuh"
 #include "pla_common.cuh"
 #include "stack_kernel.cuh"
 
@@ -35,7 +41,7 @@ struct NhwcTileGeom {
   static constexpr int THREADS = 32 * WARPS;
 };
 
-template <typename T>
+template <typename T, bool LN = false>
 struct NhwcTileSmem {
   using G = NhwcTileGeom;
   static constexpr uint32_t IN = ((G::LANES * G::SW * G::SW * sizeof(T)) + 127u) & ~127u;
@@ -43,7 +49,8 @@ struct NhwcTileSmem {
   static constexpr uint32_t OFF_IN = 0;
   static constexpr uint32_t OFF_OUT = 2 * IN;
   static constexpr uint32_t OFF_BAR = OFF_OUT + 2 * OUT;
-  static constexpr uint32_t TOTAL = OFF_BAR + 2 * sizeof(uint64_t);
+  static constexpr uint32_t OFF_LN = OFF_BAR + 2 * sizeof(uint64_t);
+  static constexpr uint32_t TOTAL = OFF_LN + (LN ? LnSmem<G::LANES, G::TS * G::TS>::BYTES : 0u);
 };
 
 struct NhwcTileArgs {
@@ -57,14 +64,15 @@ struct NhwcTileArgs {
   FastDiv div_stage_cg;  // N * tiles: stage v -> channel group v / (N * tiles)
   FastDiv div_tiles;     // tiles
   FastDiv div_tx;        // tiles_x
+  LnArgs ln;             // LN variant only
 };
 
-template <typename T>
+template <typename T, bool LN = false>
 __global__ void __launch_bounds__(NhwcTileGeom::THREADS, sizeof(T) == 2 ? 2 : 1)
     nhwc_tile_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap ymap,
                      const NhwcTileArgs a) {
   using G = NhwcTileGeom;
-  using M = NhwcTileSmem<T>;
+  using M = NhwcTileSmem<T, LN>;
   constexpr bool MIX = sizeof(T) == 2;
   constexpr int TS = G::TS, SW = G::SW, LANES = G::LANES, R = G::R;
   extern __shared__ __align__(128) unsigned char smem[];
@@ -103,8 +111,22 @@ __global__ void __launch_bounds__(NhwcTileGeom::THREADS, sizeof(T) == 2 ? 2 : 1)
     tma_load_4d(in_buf(s), &xmap, &bars[s], cg * LANES, tx * TS - kHalo, ty * TS - kHalo, n);
   };
 
-  const int v_begin = static_cast<int>((static_cast<long long>(a.stages) * blockIdx.x) / gridDim.x);
-  const int v_end = static_cast<int>((static_cast<long long>(a.stages) * (blockIdx.x + 1)) / gridDim.x);
+  // LN: the cluster's balanced range of (image, tile) units, in this rank's
+  // channel group (stage = channel group * N * tiles + unit); every rank of
+  // a cluster runs the same number of stages.
+  int v_begin, v_end;
+  int rank = 0, nranks = 1;
+  if constexpr (LN) {
+    rank = static_cast<int>(cluster_ctarank());
+    nranks = static_cast<int>(cluster_nctarank());
+    const long long units = static_cast<long long>(a.N) * a.tiles;
+    const long long cid = cluster_id_x(), ncl = nclusters_x();
+    v_begin = static_cast<int>(rank * units + (units * cid) / ncl);
+    v_end = static_cast<int>(rank * units + (units * (cid + 1)) / ncl);
+  } else {
+    v_begin = static_cast<int>((static_cast<long long>(a.stages) * blockIdx.x) / gridDim.x);
+    v_end = static_cast<int>((static_cast<long long>(a.stages) * (blockIdx.x + 1)) / gridDim.x);
+  }
   if (tid == 0 && v_begin < v_end) issue(v_begin, 0);
 
   const T* wbase = static_cast<const T*>(a.w);
@@ -113,6 +135,7 @@ __global__ void __launch_bounds__(NhwcTileGeom::THREADS, sizeof(T) == 2 ? 2 : 1)
   uint32_t wh[(kTaps + 1) / 2];
   int cur_cg = -1;
   float bias = 0.f;
+  float ln_g = 1.f, ln_b = 0.f;  // LN: scale / shift of channel 32 cg + lane
 
   for (int v = v_begin, it = 0; v < v_end; ++v, ++it) {
     const int s = it & 1;
@@ -131,6 +154,10 @@ __global__ void __launch_bounds__(NhwcTileGeom::THREADS, sizeof(T) == 2 ? 2 : 1)
         for (int t = 0; t < kTaps; ++t) wt[t] = to_acc(wbase[cw * kTaps + t]);
       }
       bias = bbase ? to_acc(bbase[cw]) : 0.f;
+      if constexpr (LN) {
+        if (a.ln.gamma) ln_g = to_acc(static_cast<const T*>(a.ln.gamma)[cw]);
+        if (a.ln.beta) ln_b = to_acc(static_cast<const T*>(a.ln.beta)[cw]);
+      }
     }
 
     mbar_wait_bounded(&bars[s], (it >> 1) & 1);
@@ -194,6 +221,10 @@ __global__ void __launch_bounds__(NhwcTileGeom::THREADS, sizeof(T) == 2 ? 2 : 1)
         os[(oy * TS + o) * LANES + lane] = from_acc<T>(val);
       }
     }
+    if constexpr (LN) {
+      ln_epilogue<T, LANES, TS * TS, G::THREADS>(os, reinterpret_cast<float*>(smem + M::OFF_LN), rank, nranks, a.C,
+                                                 a.ln.eps, a.ln.gamma != nullptr, ln_g, a.ln.beta != nullptr, ln_b);
+    }
     fence_proxy_async_smem();
     // The store that read out[s ^ 1] (issued one stage ago) is done before
     // the barrier releases the next stage's writes into it.
@@ -204,6 +235,7 @@ __global__ void __launch_bounds__(NhwcTileGeom::THREADS, sizeof(T) == 2 ? 2 : 1)
       bulk_commit();
     }
   }
+  if constexpr (LN) cluster_sync();  // peers may still read this CTA's partial sums
   if (tid == 0) bulk_wait_all();
 }
 

@@ -25,6 +25,9 @@ thread_local char g_last_cuda_error[256] = "";
 
 int cuda_fail(cudaError_t e, const char* where) {
   std::snprintf(g_last_cuda_error, sizeof(g_last_cuda_error), "%s: %s", where, cudaGetErrorString(e));
+  // Reset the runtime's last-error slot (a no-op for sticky errors), so the
+  // launch check of a later, unrelated call does not report this failure.
+  (void)cudaGetLastError();
   return PLA_ERR_CUDA;
 }
 
@@ -625,6 +628,157 @@ int launch_stack_dtype(int dtype, bool nhwc, const void* x, const void* w, const
   }
 }
 
+// ---- depthwise 7x7 + channel LayerNorm (NHWC), cluster launches ----------
+// Clusters hold one CTA per channel group; the hardware allows up to 16 CTAs
+// per cluster (more than 8 needs the non-portable opt-in).
+constexpr int kMaxClusterCtas = 16;
+
+// One-time attribute setup of a cluster kernel and the number of clusters of
+// `cs` CTAs that can be resident at once on this device (0: none fit).
+template <auto Kernel>
+int cluster_setup(int threads, uint32_t smem, int cs, int* max_clusters) {
+  int dev;
+  int st = current_device(&dev);
+  if (st != PLA_OK) return st;
+  static std::mutex mu;
+  static int cached[kMaxDevices][kMaxClusterCtas + 1] = {};  // 0: not yet known; -1: none fit
+  std::lock_guard<std::mutex> lock(mu);
+  if (cached[dev][cs] == 0) {
+    PLA_CUDA(cudaFuncSetAttribute(Kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    PLA_CUDA(cudaFuncSetAttribute(Kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = cs;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3(cs, 1, 1);
+    cfg.blockDim = dim3(threads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    PLA_CUDA(cudaOccupancyMaxActiveClusters(&n, Kernel, &cfg));
+    cached[dev][cs] = n > 0 ? n : -1;
+  }
+  *max_clusters = cached[dev][cs] > 0 ? cached[dev][cs] : 0;
+  return PLA_OK;
+}
+
+template <auto Kernel, typename Args>
+int launch_clusters(const CUtensorMap& xmap, const CUtensorMap& ymap, const Args& a, int threads, uint32_t smem,
+                    int cs, long long units, cudaStream_t stream) {
+  int max_cl = 0;
+  int st = cluster_setup<Kernel>(threads, smem, cs, &max_cl);
+  if (st != PLA_OK) return st;
+  if (max_cl == 0) {
+    std::snprintf(g_last_cuda_error, sizeof(g_last_cuda_error),
+                  "no cluster of %d CTAs (%u B shared memory each) fits on this device", cs, smem);
+    return PLA_ERR_UNSUPPORTED;
+  }
+  const long long ncl = units < max_cl ? units : max_cl;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = cs;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.gridDim = dim3(static_cast<unsigned>(cs * ncl), 1, 1);
+  cfg.blockDim = dim3(threads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  PLA_CUDA(cudaLaunchKernelEx(&cfg, Kernel, xmap, ymap, a));
+  return PLA_OK;
+}
+
+int too_many_channels(int c, int lanes) {
+  std::snprintf(g_last_cuda_error, sizeof(g_last_cuda_error),
+                "depthwise + LayerNorm: %d channels need %d CTAs per cluster, at most %d are possible", c,
+                (c + lanes - 1) / lanes, kMaxClusterCtas);
+  return PLA_ERR_UNSUPPORTED;
+}
+
+template <typename T, int S>
+int launch_stack_ln(const void* x, const void* w, const void* b, const LnArgs& ln, void* y, int dtype, int n, int c,
+                    cudaStream_t stream) {
+  using G = StackGeom<S, kMixStack<T>>;
+  using M = StackSmem<T, S, true>;
+  int st;
+  DeviceInfo* d = device_info(&st);
+  if (!d) return st;
+  if (M::TOTAL > d->smem_optin) return PLA_ERR_UNSUPPORTED;
+  const int cs = (c + G::LANES - 1) / G::LANES;
+  if (cs > kMaxClusterCtas) return too_many_channels(c, G::LANES);
+  StackArgs a;
+  a.x = x; a.w = w; a.b = b; a.y = y;
+  a.N = n; a.C = c;
+  a.planes = static_cast<long long>(n) * c;
+  a.cgroups = cs;
+  a.stages = n * cs;  // n * c < 2^31 (stack_path_ok)
+  a.full_stages = 0;
+  a.cg_major = 1;
+  a.div_c = make_fastdiv(c);
+  a.div_cg = make_fastdiv(cs);
+  a.div_n = make_fastdiv(n);
+  a.ln = ln;
+  CUtensorMap xmap, ymap;
+  st = make_nhwc_map<T>(&xmap, x, dtype, n, c, S, S, G::LANES, S);
+  if (st != PLA_OK) return st;
+  st = make_nhwc_map<T>(&ymap, y, dtype, n, c, S, S, G::LANES, S);
+  if (st != PLA_OK) return st;
+  return launch_clusters<stack_kernel<T, true, S, true>>(xmap, ymap, a, G::THREADS, M::TOTAL, cs, n, stream);
+}
+
+template <typename T>
+int launch_nhwc_tile_ln(const void* x, const void* w, const void* b, const LnArgs& ln, void* y, int dtype, int n,
+                        int c, int h, int width, cudaStream_t stream) {
+  using G = NhwcTileGeom;
+  using M = NhwcTileSmem<T, true>;
+  int st;
+  DeviceInfo* d = device_info(&st);
+  if (!d) return st;
+  const int cs = (c + G::LANES - 1) / G::LANES;
+  if (cs > kMaxClusterCtas) return too_many_channels(c, G::LANES);
+  NhwcTileArgs a;
+  a.w = w;
+  a.b = b;
+  a.N = n;
+  a.C = c;
+  a.cgroups = cs;
+  a.tiles_x = (width + G::TS - 1) / G::TS;
+  a.tiles_y = (h + G::TS - 1) / G::TS;
+  a.tiles = a.tiles_x * a.tiles_y;
+  a.stages = a.cgroups * n * a.tiles;  // < 2^31 (nhwc_tile_ok)
+  a.div_stage_cg = make_fastdiv(n * a.tiles);
+  a.div_tiles = make_fastdiv(a.tiles);
+  a.div_tx = make_fastdiv(a.tiles_x);
+  a.ln = ln;
+  CUtensorMap xmap, ymap;
+  st = make_nhwc_map<T>(&xmap, x, dtype, n, c, h, width, G::LANES, G::SW);
+  if (st != PLA_OK) return st;
+  st = make_nhwc_map<T>(&ymap, y, dtype, n, c, h, width, G::LANES, G::TS);
+  if (st != PLA_OK) return st;
+  return launch_clusters<nhwc_tile_kernel<T, true>>(xmap, ymap, a, G::THREADS, M::TOTAL, cs,
+                                                    static_cast<long long>(n) * a.tiles, stream);
+}
+
+template <typename T>
+int launch_dw_ln(const void* x, const void* w, const void* b, const LnArgs& ln, void* y, int dtype, int n, int c,
+                 int h, int width, cudaStream_t stream) {
+  if (stack_path_ok(x, y, dtype, PLA_NHWC, n, c, h, width)) {
+    switch (h) {
+      case 7: return launch_stack_ln<T, 7>(x, w, b, ln, y, dtype, n, c, stream);
+      case 14: return launch_stack_ln<T, 14>(x, w, b, ln, y, dtype, n, c, stream);
+      default: return launch_stack_ln<T, 28>(x, w, b, ln, y, dtype, n, c, stream);
+    }
+  }
+  if (nhwc_tile_ok(x, y, dtype, n, c, h, width))
+    return launch_nhwc_tile_ln<T>(x, w, b, ln, y, dtype, n, c, h, width, stream);
+  return PLA_ERR_UNSUPPORTED;
+}
+
 bool valid_dtype(int dtype) { return dtype_size(dtype) != 0; }
 
 int stencil_forward_impl(const void* x, const void* w, const void* b, const HostTaps* ht, void* y, int n, int h,
@@ -747,7 +901,8 @@ const char* pla_status_string(int status) {
 
 const char* pla_last_cuda_error(void) { return g_last_cuda_error; }
 
-int pla_version(void) { return (1 << 16) | 1; }  // 1.1: pla_depthwise_forward (k x k)
+// 1.1: pla_depthwise_forward (k x k); 1.2: pla_depthwise7x7_layernorm_nhwc
+int pla_version(void) { return (1 << 16) | 2; }
 
 int pla_stencil7x7_forward(const void* x, const void* w, const void* b, void* y, int n, int h, int width,
                            int64_t sn, int64_t sh, int64_t sw, int dtype, pla_stream_t stream) {
@@ -836,6 +991,26 @@ int pla_depthwise_forward(const void* x, const void* w, const void* b, void* y, 
   a.total = planes * plane;
   a.K = k;
   return launch_generic_dtype(dtype, a, s);
+}
+
+int pla_depthwise7x7_layernorm_nhwc(const void* x, const void* w, const void* b, const void* gamma,
+                                    const void* beta, float eps, void* y, int n, int c, int h, int width, int dtype,
+                                    pla_stream_t stream) {
+  if (dtype != PLA_F32 && dtype != PLA_BF16 && dtype != PLA_F16) return PLA_ERR_UNSUPPORTED;
+  if (n < 0 || c < 0 || h < 0 || width < 0 || !(eps >= 0.f) || eps == INFINITY) return PLA_ERR_INVALID_ARGUMENT;
+  if (static_cast<long long>(n) * c * h * width == 0) return PLA_OK;
+  if (!x || !w || !y) return PLA_ERR_INVALID_ARGUMENT;
+  if (h > (1 << 30) || width > (1 << 30)) return PLA_ERR_TOO_LARGE;
+  LnArgs ln;
+  ln.gamma = gamma;
+  ln.beta = beta;
+  ln.eps = eps;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case PLA_F32: return launch_dw_ln<float>(x, w, b, ln, y, dtype, n, c, h, width, s);
+    case PLA_BF16: return launch_dw_ln<__nv_bfloat16>(x, w, b, ln, y, dtype, n, c, h, width, s);
+    default: return launch_dw_ln<__half>(x, w, b, ln, y, dtype, n, c, h, width, s);
+  }
 }
 
 int pla_stencil7x7_band_step(const void* in, const void* w, const void* b, void* out, int rows, int width,

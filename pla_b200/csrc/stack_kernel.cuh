@@ -31,8 +31,13 @@
 //    raw buffer (free once F holds it); 16-bit stacks, which read the raw
 //    buffer while computing, write to a 2-buffer output ring instead, so one
 //    barrier per stage suffices.
+//  * LN (NHWC only): the stage's outputs go through the channel LayerNorm
+//    epilogue of ln_epilogue.cuh before the store.  The kernel then runs as
+//    clusters of C / LANES CTAs: rank r owns channel group r of the images
+//    the cluster visits, so its filters never change.
 #pragma once
 
+#include "ln_epilogue.cuh"
 #include "pla_common.cuh"
 
 namespace pla {
@@ -55,7 +60,7 @@ struct StackGeom {
 template <typename T>
 constexpr bool kMixStack = sizeof(T) == 2;
 
-template <typename T, int S>
+template <typename T, int S, bool LN = false>
 struct StackSmem {
   using G = StackGeom<S, kMixStack<T>>;
   static constexpr uint32_t RAW = ((G::LANES * S * S * sizeof(T)) + 127u) & ~127u;
@@ -65,7 +70,8 @@ struct StackSmem {
   // 16-bit stacks write outputs to their own 2-buffer ring (no in-place reuse).
   static constexpr uint32_t OFF_OUT = OFF_RAW + 2 * RAW;
   static constexpr uint32_t OFF_BAR = OFF_OUT + (kMixStack<T> ? 2 * RAW : 0u);
-  static constexpr uint32_t TOTAL = OFF_BAR + 2 * sizeof(uint64_t);
+  static constexpr uint32_t OFF_LN = OFF_BAR + 2 * sizeof(uint64_t);
+  static constexpr uint32_t TOTAL = OFF_LN + (LN ? LnSmem<G::LANES, S * S>::BYTES : 0u);
 };
 
 struct StackArgs {
@@ -80,6 +86,7 @@ struct StackArgs {
   int full_stages;     // NCHW: stages whose chunk is complete (bulk-copy path)
   int cg_major;        // 1: visit stages channel-group-major (see stage_of)
   FastDiv div_c, div_cg, div_n;
+  LnArgs ln;           // LN variant only
 };
 
 // CTAs own contiguous ranges of "virtual" stages.  With cg_major, virtual
@@ -132,13 +139,16 @@ __device__ __forceinline__ float raw_to_f(float v) { return v; }
 __device__ __forceinline__ float raw_to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
 __device__ __forceinline__ float raw_to_f(__half v) { return __half2float(v); }
 
-template <typename T, bool NHWC, int S>
+template <typename T, bool NHWC, int S, bool LN = false>
 __global__ void __launch_bounds__(StackGeom<S, kMixStack<T>>::THREADS, StackGeom<S, kMixStack<T>>::MIN_BLOCKS)
     stack_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap ymap,
                  const StackArgs a) {
+  static_assert(!LN || NHWC, "the LayerNorm epilogue normalises the channels of NHWC pixels");
+  // The epilogue's thread t handles channel t % LANES, which must be lane ln.
+  static_assert(StackGeom<S, kMixStack<T>>::G == 1 || StackGeom<S, kMixStack<T>>::RG == 1, "ln == tid % LANES");
   constexpr bool MIX = kMixStack<T>;
   using G = StackGeom<S, MIX>;
-  using M = StackSmem<T, S>;
+  using M = StackSmem<T, S, LN>;
   constexpr int R = G::R, Q = G::Q, LANES = G::LANES;
   extern __shared__ __align__(128) unsigned char smem[];
   float* F = reinterpret_cast<float*>(smem + M::OFF_F);
@@ -184,9 +194,22 @@ __global__ void __launch_bounds__(StackGeom<S, kMixStack<T>>::THREADS, StackGeom
     }
   };
 
-  // Balanced contiguous range of virtual stages for this CTA.
-  const int v_begin = static_cast<int>((static_cast<long long>(a.stages) * blockIdx.x) / gridDim.x);
-  const int v_end = static_cast<int>((static_cast<long long>(a.stages) * (blockIdx.x + 1)) / gridDim.x);
+  // Balanced contiguous range of virtual stages for this CTA.  LN: the
+  // cluster's balanced range of images, in this rank's channel group
+  // (virtual stage = channel group * N + image); every rank of a cluster
+  // runs the same number of stages.
+  int v_begin, v_end;
+  int rank = 0, nranks = 1;
+  if constexpr (LN) {
+    rank = static_cast<int>(cluster_ctarank());
+    nranks = static_cast<int>(cluster_nctarank());
+    const long long cid = cluster_id_x(), ncl = nclusters_x();
+    v_begin = rank * a.N + static_cast<int>((static_cast<long long>(a.N) * cid) / ncl);
+    v_end = rank * a.N + static_cast<int>((static_cast<long long>(a.N) * (cid + 1)) / ncl);
+  } else {
+    v_begin = static_cast<int>((static_cast<long long>(a.stages) * blockIdx.x) / gridDim.x);
+    v_end = static_cast<int>((static_cast<long long>(a.stages) * (blockIdx.x + 1)) / gridDim.x);
+  }
   if (tid == 0 && v_begin < v_end) issue(stage_of(v_begin, a), 0);
 
   const T* wbase = static_cast<const T*>(a.w);
@@ -195,6 +218,7 @@ __global__ void __launch_bounds__(StackGeom<S, kMixStack<T>>::THREADS, StackGeom
   uint32_t wh[(kTaps + 1) / 2];
   int cur_c = -1;
   float bias = 0.f;
+  float ln_g = 1.f, ln_b = 0.f;  // LN: this thread's channel scale / shift (step 5)
 
   for (int v = v_begin, it = 0; v < v_end; ++v, ++it) {
     const int s = it & 1;
@@ -230,6 +254,10 @@ __global__ void __launch_bounds__(StackGeom<S, kMixStack<T>>::THREADS, StackGeom
         for (int t = 0; t < kTaps; ++t) wt[t] = to_acc(wbase[cw * kTaps + t]);
       }
       bias = bbase ? to_acc(bbase[cw]) : 0.f;
+      if constexpr (LN) {
+        if (a.ln.gamma) ln_g = to_acc(static_cast<const T*>(a.ln.gamma)[cw]);
+        if (a.ln.beta) ln_b = to_acc(static_cast<const T*>(a.ln.beta)[cw]);
+      }
     }
 
     // ---- raw stage in shared memory ------------------------------------
@@ -364,6 +392,12 @@ __global__ void __launch_bounds__(StackGeom<S, kMixStack<T>>::THREADS, StackGeom
           os[ln * PLANE + oy * S + o] = e;
       }
     }
+    if constexpr (LN) {
+      // In the epilogue thread t handles channel t % LANES: the same lane ln
+      // (THREADS = LANES x row groups), whose scale and shift it holds.
+      ln_epilogue<T, LANES, S * S, G::THREADS>(os, reinterpret_cast<float*>(smem + M::OFF_LN), rank, nranks, a.C,
+                                               a.ln.eps, a.ln.gamma != nullptr, ln_g, a.ln.beta != nullptr, ln_b);
+    }
     fence_proxy_async_smem();
     // 16-bit: before this barrier releases the next stage's writes into
     // out[s ^ 1], the bulk store that read it (issued one stage ago) is done.
@@ -385,6 +419,7 @@ __global__ void __launch_bounds__(StackGeom<S, kMixStack<T>>::THREADS, StackGeom
     }
     (void)lane_ok;
   }
+  if constexpr (LN) cluster_sync();  // peers may still read this CTA's partial sums
   if (tid == 0) bulk_wait_all();
 }
 

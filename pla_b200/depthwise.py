@@ -92,6 +92,69 @@ def depthwise_kxk(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | No
     return out
 
 
+def depthwise7x7_layernorm(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None,
+                           norm_weight: torch.Tensor | None = None, norm_bias: torch.Tensor | None = None,
+                           eps: float = 1e-6, out: torch.Tensor | None = None) -> torch.Tensor:
+    """LayerNorm over channels of depthwise7x7(x), fused into one pass (ConvNeXt's dwconv -> norm).
+
+    ``x`` is a channels_last CUDA tensor [N, C, H, W] (fp32 / bf16 / fp16);
+    the result is channels_last too, so ``result.permute(0, 2, 3, 1)`` is the
+    contiguous [N, H, W, C] tensor that ``nn.LayerNorm(C)`` returns in a
+    ConvNeXt block.  ``weight`` [C,1,7,7], ``bias`` / ``norm_weight`` /
+    ``norm_bias`` [C] or None, all of x's dtype.  The normalisation works on
+    the depthwise outputs rounded to x's dtype (what the unfused pair sees)
+    in fp32.  No reference counterpart: the reference's operator is the
+    depthwise half (data/depthwise_conv_7x7.py:15-29).
+    """
+    if not isinstance(x, torch.Tensor) or not x.is_cuda:
+        raise ValueError("depthwise7x7_layernorm requires a CUDA input")
+    if x.dim() != 4:
+        raise RuntimeError("input must have shape [N,C,H,W]")
+    if not x.is_contiguous(memory_format=torch.channels_last):
+        raise RuntimeError("depthwise7x7_layernorm normalises NHWC pixels: pass a channels_last input")
+    N, C, H, W = x.shape
+    if x.dtype not in (torch.float32, torch.bfloat16, torch.float16):
+        raise RuntimeError("unsupported dtype")
+    if not weight.is_cuda or weight.device != x.device or weight.dtype != x.dtype or weight.numel() != C * 49:
+        raise RuntimeError("weight must be a [C,1,7,7] CUDA tensor of x's dtype on x's device")
+    for name, t in (("bias", bias), ("norm_weight", norm_weight), ("norm_bias", norm_bias)):
+        if t is not None and (not t.is_cuda or t.device != x.device or t.dtype != x.dtype or t.numel() != C):
+            raise RuntimeError(f"{name} device/dtype/shape mismatch")
+    if out is None:
+        out = torch.empty(x.shape, dtype=x.dtype, device=x.device, memory_format=torch.channels_last)
+    elif out.shape != x.shape or not out.is_contiguous(memory_format=torch.channels_last) or out.dtype != x.dtype:
+        raise RuntimeError("out must match x's shape, dtype and channels_last format")
+    if out.numel() == 0:
+        return out
+    vecs = [None if t is None else t.detach().contiguous() for t in (bias, norm_weight, norm_bias)]
+    weight = weight.detach().contiguous()
+    with torch.cuda.device(x.device):
+        st = _lib.lib().pla_depthwise7x7_layernorm_nhwc(
+            x.data_ptr(), weight.data_ptr(), _lib.ptr(vecs[0]), _lib.ptr(vecs[1]), _lib.ptr(vecs[2]), float(eps),
+            out.data_ptr(), N, C, H, W, _lib.DTYPE_CODE[x.dtype], _lib.stream_ptr(x.device))
+    _lib.check(st, "pla_depthwise7x7_layernorm_nhwc")
+    return out
+
+
+class DepthwiseLayerNorm(torch.nn.Module):
+    """ConvNeXt block head: ``dwconv`` (7x7 depthwise, bias) then ``norm`` (LayerNorm over C), fused.
+
+    Parameter names follow the ConvNeXt block (``dwconv.weight`` [C,1,7,7],
+    ``dwconv.bias`` [C], ``norm.weight`` / ``norm.bias`` [C]), so its state
+    dict slots into one.  ``forward`` takes a channels_last [N, C, H, W]
+    tensor and returns the normalised channels_last tensor.
+    """
+
+    def __init__(self, dim: int, eps: float = 1e-6, bias: bool = True):
+        super().__init__()
+        self.dwconv = torch.nn.Conv2d(dim, dim, 7, padding=3, groups=dim, bias=bias)
+        self.norm = torch.nn.LayerNorm(dim, eps=eps)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        return depthwise7x7_layernorm(x, self.dwconv.weight, self.dwconv.bias, self.norm.weight, self.norm.bias,
+                                      self.norm.eps)
+
+
 class ModelNew(torch.nn.Module):
     """KernelBench drop-in for data/depthwise_conv_7x7.py's Model (parameter ``conv2d``).
 

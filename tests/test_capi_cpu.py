@@ -125,3 +125,27 @@ def test_bench_reads_profiled_traffic():
     t, src = bench.profiled_traffic("stencil7x7_cfg2_4096x4096_f32")
     assert t and t > 60e6 and src.endswith(".md")
     assert bench.profiled_traffic("no-such-workload") == (None, None)
+
+
+def test_depthwise_layernorm_validates_without_device():
+    from pla_b200 import _lib
+
+    L = _lib.lib()
+    f = L.pla_depthwise7x7_layernorm_nhwc
+    assert f(None, None, None, None, None, 1e-6, None, 1, 32, 7, 7, 2, None) == 2  # fp64
+    assert f(None, None, None, None, None, 1e-6, None, -1, 32, 7, 7, 1, None) == 1  # negative size
+    assert f(None, None, None, None, None, -1.0, None, 1, 32, 7, 7, 1, None) == 1  # negative eps
+    assert f(None, None, None, None, None, float("nan"), None, 1, 32, 7, 7, 1, None) == 1
+    assert f(None, None, None, None, None, 1e-6, None, 1, 32, 7, 7, 1, None) == 1  # NULL buffers
+    assert f(None, None, None, None, None, 1e-6, None, 0, 32, 7, 7, 1, None) == 0  # empty
+
+
+def test_depthwise_layernorm_module_interface():
+    from pla_b200 import DepthwiseLayerNorm
+
+    m = DepthwiseLayerNorm(96)
+    # ConvNeXt block names: dwconv (7x7 depthwise with bias), norm (LayerNorm over C)
+    assert set(m.state_dict()) == {"dwconv.weight", "dwconv.bias", "norm.weight", "norm.bias"}
+    assert tuple(m.dwconv.weight.shape) == (96, 1, 7, 7) and m.norm.eps == 1e-6
+    with pytest.raises(ValueError):
+        m(torch.rand(1, 96, 7, 7).contiguous(memory_format=torch.channels_last))

@@ -78,3 +78,58 @@ def test_oracle_threads_do_not_change_results():
     a = oracle.depthwise7x7(x, w, b, threads=1)
     c = oracle.depthwise7x7(x, w, b, threads=7)
     assert torch.equal(a, c)
+
+
+# --------------------------------------------------------------------------
+# depthwise 7x7 + channel LayerNorm (NHWC).  No reference counterpart: the
+# LayerNorm half is pinned to torch's own F.layer_norm on the reference
+# depthwise module's output (data/depthwise_conv_7x7.py:15-29 run through
+# oracle/reference_modules.py), the depthwise half to the golden vectors above.
+# --------------------------------------------------------------------------
+def _torch_dw_ln(x, w, b, gamma, beta, eps):
+    import torch.nn.functional as F
+
+    C = x.shape[1]
+    y = F.conv2d(x.float(), w.float(), None if b is None else b.float(), padding=3, groups=C).to(x.dtype)
+    z = F.layer_norm(y.float().permute(0, 2, 3, 1), (C,), None if gamma is None else gamma.float(),
+                     None if beta is None else beta.float(), eps)
+    return z.permute(0, 3, 1, 2).to(x.dtype)
+
+
+@pytest.mark.parametrize("dtype,tol", [(torch.float32, 1e-5), (torch.bfloat16, 2e-2), (torch.float16, 2e-2)])
+@pytest.mark.parametrize("shape", [(2, 96, 14, 14), (1, 40, 7, 7), (2, 72, 20, 20), (1, 200, 7, 7)])
+@pytest.mark.parametrize("affine", [True, False])
+def test_oracle_depthwise_layernorm_matches_torch(dtype, tol, shape, affine):
+    g = torch.Generator().manual_seed(hash((shape, affine)) % 1000)
+    N, C, H, W = shape
+    x = torch.randn(*shape, generator=g).to(dtype)
+    w = (torch.randn(C, 1, 7, 7, generator=g) / 7).to(dtype)
+    b = (torch.randn(C, generator=g) * 0.1).to(dtype) if affine else None
+    gamma = (1 + 0.2 * torch.randn(C, generator=g)).to(dtype) if affine else None
+    beta = (0.1 * torch.randn(C, generator=g)).to(dtype) if affine else None
+    got = oracle.depthwise7x7_layernorm(x, w, b, gamma, beta, 1e-6)
+    assert got.is_contiguous(memory_format=torch.channels_last)
+    ref = _torch_dw_ln(x, w, b, gamma, beta, 1e-6)
+    torch.testing.assert_close(got.float(), ref.float(), rtol=tol, atol=tol)
+    # the depthwise half is the plain oracle's output
+    if not affine:
+        y = oracle.depthwise7x7(x.contiguous(memory_format=torch.channels_last), w, None)
+        assert torch.equal(got, oracle.depthwise7x7_layernorm(y.contiguous(memory_format=torch.channels_last),
+                                                              _identity_filter(C, dtype), None, None, None, 1e-6))
+
+
+def _identity_filter(C, dtype):
+    w = torch.zeros(C, 1, 7, 7)
+    w[:, 0, 3, 3] = 1.0
+    return w.to(dtype)
+
+
+def test_oracle_depthwise_layernorm_constant_pixels():
+    # A pixel whose channels are all equal has zero variance: z = beta exactly.
+    C = 64
+    x = torch.zeros(1, C, 7, 7)
+    w = torch.zeros(C, 1, 7, 7)
+    b = torch.full((C,), 0.75)
+    beta = torch.linspace(-1, 1, C)
+    z = oracle.depthwise7x7_layernorm(x, w, b, torch.ones(C), beta, 1e-6)
+    assert torch.equal(z, beta.view(1, C, 1, 1).expand(1, C, 7, 7).contiguous(memory_format=torch.channels_last))
