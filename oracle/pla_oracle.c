@@ -240,17 +240,36 @@ int oracle_stencil7x7_iterate_f32(const float* x, const float* w, const float* b
  *
  * Images [n0, n1).  The depthwise output is exactly oracle_depthwise's (one
  * rounding to dtype); the normalisation then reads those rounded values v_c
- * (widened to fp32) and evaluates, per pixel, in this fixed order:
- *   S    = sum over 32-channel groups g = 0, 1, ... of P_g, where
- *          P_g = sum of v_c over the group's channels in ascending order,
- *          both sums starting from +0 (separate adds, no fusion)
- *   mean = S / C
- *   M    = the same grouping over d_c * d_c, d_c = v_c - mean
+ * (widened to fp32) and evaluates, per pixel, in this fixed order, with the
+ * channels split into 32-channel groups g (n_g channels each; the last group
+ * may be shorter) and every sum running in ascending order from +0:
+ *   s_g  = sum of v_c over group g
+ *   m_g  = s_g / n_g
+ *   q_g  = sum over group g of d * d, d = v_c - m_g
+ *   mean = (sum over g of s_g) / C
+ *   M    = sum over g of (q_g + n_g * (e * e)), e = m_g - mean
+ *          (the groups' squared deviations combined by Chan, Golub and
+ *           LeVeque's pairwise-update formula)
  *   inv  = 1 / sqrt(M / C + eps)
- *   z_c  = ((d_c * inv) * gamma_c) + beta_c   (gamma / beta skipped if NULL)
- * every operation correctly rounded fp32, then one rounding of z_c to dtype.
- * The CUDA epilogue evaluates the same expression tree.
+ *   z_c  = ((v_c - mean) * inv) * gamma_c + beta_c   (gamma / beta skipped if NULL)
+ * every operation a correctly rounded fp32 add / multiply / divide / square
+ * root, then one rounding of z_c to dtype.  The CUDA epilogue evaluates the
+ * same expression tree (a group is what one CTA reduces locally before the
+ * CTAs of a cluster exchange their partial results).
  */
+static void group_stats(const void* y, int64_t base, int g, int n, int dtype, float* s_out, float* q_out) {
+  float s = 0.0f;
+  for (int c = g; c < g + n; ++c) s = s + load_f(y, base + c, dtype);
+  const float m = s / (float)n;
+  float q = 0.0f;
+  for (int c = g; c < g + n; ++c) {
+    const float d = load_f(y, base + c, dtype) - m;
+    q = q + d * d;
+  }
+  *s_out = s;
+  *q_out = q;
+}
+
 int oracle_depthwise7x7_layernorm_nhwc(const void* x, const void* w, const void* b, const void* gamma,
                                        const void* beta, float eps, void* y, int N, int C, int H, int W,
                                        int dtype, int n0, int n1) {
@@ -265,19 +284,18 @@ int oracle_depthwise7x7_layernorm_nhwc(const void* x, const void* w, const void*
     const int64_t base = px * C;
     float s = 0.0f;
     for (int g = 0; g < C; g += 32) {
-      float part = 0.0f;
-      for (int c = g; c < C && c < g + 32; ++c) part = part + load_f(y, base + c, dtype);
-      s = s + part;
+      float sg, qg;
+      group_stats(y, base, g, C - g < 32 ? C - g : 32, dtype, &sg, &qg);
+      s = s + sg;
     }
     const float mean = s / fc;
     float m = 0.0f;
     for (int g = 0; g < C; g += 32) {
-      float part = 0.0f;
-      for (int c = g; c < C && c < g + 32; ++c) {
-        const float d = load_f(y, base + c, dtype) - mean;
-        part = part + d * d;
-      }
-      m = m + part;
+      const int n = C - g < 32 ? C - g : 32;
+      float sg, qg;
+      group_stats(y, base, g, n, dtype, &sg, &qg);
+      const float e = sg / (float)n - mean;
+      m = m + (qg + (float)n * (e * e));
     }
     const float inv = 1.0f / sqrtf(m / fc + eps);
     for (int c = 0; c < C; ++c) {

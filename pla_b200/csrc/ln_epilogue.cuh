@@ -7,31 +7,38 @@
 // shared memory ("os", element (p, l) at os[p * LANES + l]).  LayerNorm needs
 // all C channels of a pixel, so the kernels run as thread-block clusters: the
 // CTA of cluster rank r owns channels [r * LANES, (r + 1) * LANES) of the
-// same pixels, and the per-pixel partial sums travel between the CTAs
-// through distributed shared memory (mapa + ld.shared::cluster), with two
-// cluster barriers per stage:
+// same pixels, and per-pixel partial results travel between the CTAs through
+// distributed shared memory (mapa + ld.shared::cluster), one exchange per
+// stage:
 //
-//   1. each CTA sums its channels of every pixel, per 32-channel group, in
-//      ascending channel order -> part[g][p];
-//   2. barrier; every CTA reads all ranks' partials of its pixels and adds
-//      them in channel-group order -> mean = S / C;
-//   3. each CTA sums (v - mean)^2 the same way -> part2[g][p];
-//   4. barrier; every CTA adds all partials -> inv = 1 / sqrt(M / C + eps);
-//   5. z = ((v - mean) * inv) * gamma + beta, written back into os (the
-//      kernel's TMA store then sends it out).
+//   ln_local_stats  each CTA reduces every (32-channel group, pixel) of its
+//                   stage on its own: sum s_g and, around the group mean
+//                   m_g = s_g / n_g, the sum of squared deviations q_g;
+//                   -> part[buf][g][p], part2[buf][g][p]; then the cluster
+//                   barrier is ARRIVED at (release);
+//   ln_combine      after the barrier's WAIT (acquire), every CTA loads all
+//                   groups' (s_g, q_g) of its pixels from the owning ranks,
+//                   eight loads in flight at a time, and combines them in
+//                   group order: mean = sum s_g / C,
+//                   M = sum (q_g + n_g (m_g - mean)^2)  (Chan, Golub and
+//                   LeVeque's pairwise variance update: stable, one exchange),
+//                   inv = 1 / sqrt(M / C + eps);
+//   ln_normalize    z = ((v - mean) * inv) * gamma + beta, in place in os.
 //
 // Every operation is a correctly rounded fp32 add / multiply / divide /
-// square root in a fixed tree (the CPU oracle's
-// oracle_depthwise7x7_layernorm_nhwc restates it), so the result is the same
-// bit for bit.  v is the depthwise output already rounded to T, exactly what
-// the unfused pair would hand to the LayerNorm.
+// square root in a fixed tree, which the CPU oracle's
+// oracle_depthwise7x7_layernorm_nhwc restates, so the result is the same bit
+// for bit.  v is the depthwise output already rounded to T, exactly what the
+// unfused pair would hand to the LayerNorm.
 //
-// Reuse of part / part2 across stages needs no third barrier: a peer reads a
-// CTA's part[] between barrier 1 and its own arrival at barrier 2 of the same
-// stage, and the owner rewrites part[] only after barrier 2; part2[] is read
-// between barrier 2 and the next stage's barrier 1 and rewritten after that
-// barrier.  The kernels end with one more cluster barrier so that no CTA
-// exits while a peer may still read its shared memory.
+// Kernels with an output ring split the barrier around the next stage's
+// FMAs (arrive after stage i's local statistics, wait after stage i+1's
+// convolution), so the exchange's latency hides behind compute; stage i is
+// normalised and stored then.  part / part2 alternate between two buffers by
+// stage parity: a peer reads stage i's buffer between wait(i) and its own
+// arrive(i + 1), and the owner rewrites it at stage i + 2, after wait(i + 1).
+// The kernels end with one more cluster barrier so that no CTA exits while
+// a peer may still read its shared memory.
 #pragma once
 
 #include "pla_common.cuh"
@@ -64,12 +71,18 @@ __device__ __forceinline__ uint32_t nclusters_x() {
   asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
   return r;
 }
-// All threads of all CTAs of the cluster; release / acquire orders the
-// shared-memory writes before it against the peers' reads after it.
+// Cluster barrier halves; every thread of every CTA of the cluster executes
+// them, alternating arrive / wait.  Release / acquire order the shared-memory
+// writes before an arrive against the peers' reads after their wait.
+__device__ __forceinline__ void cluster_arrive() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
 __device__ __forceinline__ void cluster_sync() {
-  asm volatile(
-      "barrier.cluster.arrive.release.aligned;\n\t"
-      "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+  cluster_arrive();
+  cluster_wait();
 }
 // Shared-memory address `addr` of this CTA -> the same offset in cluster rank `rank`.
 __device__ __forceinline__ uint32_t dsmem_map(uint32_t addr, uint32_t rank) {
@@ -83,107 +96,136 @@ __device__ __forceinline__ float dsmem_ld(uint32_t addr) {
   return v;
 }
 
-// Shared-memory footprint of the epilogue: part[GL][P], part2[GL][P], mean[P], inv[P].
+// Shared memory of the epilogue: part[2][GL][P], part2[2][GL][P] (two
+// buffers by stage parity), mean[P], inv[P].
 template <int LANES, int P>
 struct LnSmem {
   static constexpr int GL = LANES / 32;
-  static constexpr uint32_t BYTES = static_cast<uint32_t>((2 * GL * P + 2 * P) * sizeof(float));
+  static constexpr uint32_t BYTES = static_cast<uint32_t>((4 * GL * P + 2 * P) * sizeof(float));
 };
 
-// Sum of v (or of (v - mean)^2 when SQ) over channels [0, nv) of one 32-channel
-// group of one pixel, in ascending order from +0.  `row` is 16-byte aligned.
-template <typename T, bool SQ>
-__device__ __forceinline__ float group_sum(const T* row, int nv, float mean) {
+template <int LANES, int P>
+struct LnView {
+  static constexpr int GL = LANES / 32;
+  float* base;
+  __device__ float* part(int buf) const { return base + buf * GL * P; }
+  __device__ float* part2(int buf) const { return base + (2 + buf) * GL * P; }
+  __device__ float* mean() const { return base + 4 * GL * P; }
+  __device__ float* inv() const { return base + 4 * GL * P + P; }
+};
+
+// Channels of 32-channel group `gi` of this CTA's stage that exist (0..32).
+__device__ __forceinline__ int group_size(int C, int c0, int gi) {
+  const int n = C - c0 - gi * 32;
+  return n < 0 ? 0 : (n > 32 ? 32 : n);
+}
+
+// (s_g, q_g) of every (group, pixel) of the stage in os -> part[buf], part2[buf].
+template <typename T, int LANES, int P, int THREADS>
+__device__ __forceinline__ void ln_local_stats(const T* os, const LnView<LANES, P>& v, int buf, int c0, int C) {
+  constexpr int GL = LANES / 32;
   constexpr int VEC = 16 / sizeof(T);
-  float s = 0.f;
+  float* part = v.part(buf);
+  float* part2 = v.part2(buf);
+  for (int t = threadIdx.x; t < GL * P; t += THREADS) {
+    const int gi = t / P, p = t - gi * P;
+    const int n = group_size(C, c0, gi);
+    const uint4* row = reinterpret_cast<const uint4*>(os + p * LANES + gi * 32);  // 16-byte aligned
+    float x[32];
 #pragma unroll
-  for (int q = 0; q < 32 / VEC; ++q) {
-    const uint4 u = reinterpret_cast<const uint4*>(row)[q];
-    const T* e = reinterpret_cast<const T*>(&u);
+    for (int q = 0; q < 32 / VEC; ++q) {
+      const uint4 u = row[q];
+      const T* e = reinterpret_cast<const T*>(&u);
 #pragma unroll
-    for (int j = 0; j < VEC; ++j) {
-      if (q * VEC + j < nv) {
-        const float v = to_acc(e[j]);
-        if (SQ) {
-          const float d = __fsub_rn(v, mean);
-          s = __fadd_rn(s, __fmul_rn(d, d));
-        } else {
-          s = __fadd_rn(s, v);
+      for (int j = 0; j < VEC; ++j) x[q * VEC + j] = to_acc(e[j]);
+    }
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (j < n) s = __fadd_rn(s, x[j]);
+    float q2 = 0.f;
+    if (n > 0) {
+      const float m = __fdiv_rn(s, static_cast<float>(n));
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        if (j < n) {
+          const float d = __fsub_rn(x[j], m);
+          q2 = __fadd_rn(q2, __fmul_rn(d, d));
         }
       }
     }
+    part[t] = s;
+    part2[t] = q2;
   }
-  return s;
 }
 
-// The epilogue (all threads of the CTA call it, the same number of times in
-// every CTA of the cluster).  os: the stage's LANES x P outputs (rounded to
-// T); ln_smem: LnSmem<LANES, P>::BYTES of 16-byte aligned shared memory;
-// rank / nranks: this CTA's cluster rank and the cluster size; C: channels.
-// Thread tid always handles channel tid % LANES in step 5 (THREADS is a
-// multiple of LANES), whose scale and shift the caller passes in g / bt.
-template <typename T, int LANES, int P, int THREADS>
-__device__ __forceinline__ void ln_epilogue(T* os, float* ln_smem, int rank, int nranks, int C, float eps,
-                                            bool has_gamma, float g, bool has_beta, float bt) {
-  static_assert(LANES % 32 == 0 && THREADS % LANES == 0, "fixed channel per thread");
+// After cluster_wait(): mean and 1 / sqrt(var + eps) of every pixel of the
+// stage whose partials are in buffer `buf` of every rank -> v.mean(), v.inv().
+template <int LANES, int P, int THREADS>
+__device__ __forceinline__ void ln_combine(const LnView<LANES, P>& v, int buf, int C, float eps) {
   constexpr int GL = LANES / 32;
-  float* part = ln_smem;
-  float* part2 = part + GL * P;
-  float* mean_s = part2 + GL * P;
-  float* inv_s = mean_s + P;
-  const int tid = threadIdx.x;
-  const int c0 = rank * LANES;
-  const int ngroups = (C + 31) / 32;  // 32-channel groups over all ranks
+  constexpr int CH = 8;  // remote loads in flight per thread
+  const int ngroups = (C + 31) / 32;
   const float fc = static_cast<float>(C);
-
-  __syncthreads();  // os complete
-  // 1. partial sums per (group, pixel)
-  for (int t = tid; t < GL * P; t += THREADS) {
-    const int gi = t / P, p = t - gi * P;
-    part[t] = group_sum<T, false>(os + p * LANES + gi * 32, C - c0 - gi * 32, 0.f);
-  }
-  cluster_sync();
-  // 2. mean per pixel: all ranks' partials in channel-group order
-  const uint32_t part_a = smem_u32(part), part2_a = smem_u32(part2);
-  for (int p = tid; p < P; p += THREADS) {
+  const uint32_t pa = smem_u32(v.part(buf)), qa = smem_u32(v.part2(buf));
+  float* mean_s = v.mean();
+  float* inv_s = v.inv();
+  for (int p = threadIdx.x; p < P; p += THREADS) {
     float s = 0.f;
-    for (int r = 0; r < nranks; ++r) {
+    for (int g0 = 0; g0 < ngroups; g0 += CH) {
+      float sv[CH];
 #pragma unroll
-      for (int gi = 0; gi < GL; ++gi) {
-        if (r * GL + gi < ngroups) s = __fadd_rn(s, dsmem_ld(dsmem_map(part_a + (gi * P + p) * 4u, r)));
+      for (int j = 0; j < CH; ++j) {
+        const int g = g0 + j;
+        sv[j] = g < ngroups ? dsmem_ld(dsmem_map(pa + ((g % GL) * P + p) * 4u, g / GL)) : 0.f;
+      }
+#pragma unroll
+      for (int j = 0; j < CH; ++j)
+        if (g0 + j < ngroups) s = __fadd_rn(s, sv[j]);
+    }
+    const float mean = __fdiv_rn(s, fc);
+    float m2 = 0.f;
+    for (int g0 = 0; g0 < ngroups; g0 += CH) {
+      float sv[CH], qv[CH];
+#pragma unroll
+      for (int j = 0; j < CH; ++j) {
+        const int g = g0 + j;
+        const uint32_t off = ((g % GL) * P + p) * 4u;
+        sv[j] = g < ngroups ? dsmem_ld(dsmem_map(pa + off, g / GL)) : 0.f;
+        qv[j] = g < ngroups ? dsmem_ld(dsmem_map(qa + off, g / GL)) : 0.f;
+      }
+#pragma unroll
+      for (int j = 0; j < CH; ++j) {
+        const int g = g0 + j;
+        if (g < ngroups) {
+          const int n = C - g * 32 < 32 ? C - g * 32 : 32;
+          const float fn = static_cast<float>(n);
+          const float e = __fsub_rn(__fdiv_rn(sv[j], fn), mean);
+          m2 = __fadd_rn(m2, __fadd_rn(qv[j], __fmul_rn(fn, __fmul_rn(e, e))));
+        }
       }
     }
-    mean_s[p] = __fdiv_rn(s, fc);
+    mean_s[p] = mean;
+    inv_s[p] = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(m2, fc), eps)));
   }
-  __syncthreads();
-  // 3. partial sums of squared deviations
-  for (int t = tid; t < GL * P; t += THREADS) {
-    const int gi = t / P, p = t - gi * P;
-    part2[t] = group_sum<T, true>(os + p * LANES + gi * 32, C - c0 - gi * 32, mean_s[p]);
-  }
-  cluster_sync();
-  // 4. 1 / sqrt(var + eps) per pixel
-  for (int p = tid; p < P; p += THREADS) {
-    float m = 0.f;
-    for (int r = 0; r < nranks; ++r) {
-#pragma unroll
-      for (int gi = 0; gi < GL; ++gi) {
-        if (r * GL + gi < ngroups) m = __fadd_rn(m, dsmem_ld(dsmem_map(part2_a + (gi * P + p) * 4u, r)));
-      }
-    }
-    inv_s[p] = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(m, fc), eps)));
-  }
-  __syncthreads();
-  // 5. normalise in place
-  const int l = tid % LANES;
-  if (c0 + l < C) {
-    for (int i = tid; i < P * LANES; i += THREADS) {
-      const int p = i / LANES;
-      float t = __fmul_rn(__fsub_rn(to_acc(os[i]), mean_s[p]), inv_s[p]);
-      if (has_gamma) t = __fmul_rn(t, g);
-      if (has_beta) t = __fadd_rn(t, bt);
-      os[i] = from_acc<T>(t);
-    }
+}
+
+// z = ((v - mean) * inv) * gamma + beta in place.  Thread tid handles channel
+// c0 + tid % LANES (THREADS is a multiple of LANES), whose scale and shift it
+// holds in g / bt.
+template <typename T, int LANES, int P, int THREADS>
+__device__ __forceinline__ void ln_normalize(T* os, const LnView<LANES, P>& v, int c0, int C, bool has_gamma,
+                                             float g, bool has_beta, float bt) {
+  static_assert(LANES % 32 == 0 && THREADS % LANES == 0, "fixed channel per thread");
+  const float* mean_s = v.mean();
+  const float* inv_s = v.inv();
+  if (c0 + static_cast<int>(threadIdx.x % LANES) >= C) return;
+  for (int i = threadIdx.x; i < P * LANES; i += THREADS) {
+    const int p = i / LANES;
+    float t = __fmul_rn(__fsub_rn(to_acc(os[i]), mean_s[p]), inv_s[p]);
+    if (has_gamma) t = __fmul_rn(t, g);
+    if (has_beta) t = __fadd_rn(t, bt);
+    os[i] = from_acc<T>(t);
   }
 }
 

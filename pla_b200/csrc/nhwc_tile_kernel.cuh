@@ -23,7 +23,8 @@
 // LN: the stage's outputs go through the channel LayerNorm epilogue of
 // ln_epilogue.cuh before the store; the kernel then runs as clusters of
 // ceil(C / 32) CTAs, rank r taking channel group r of the (image, tile)
-// stages its cluster visits.
+// stages its cluster visits.  A stage is normalised and stored one stage
+// late, so the cluster exchange overlaps the next stage's FMAs.
 #pragma once
 
 #include "ln_epilogue.cuh"
@@ -115,10 +116,9 @@ __global__ void __launch_bounds__(NhwcTileGeom::THREADS, sizeof(T) == 2 ? 2 : 1)
   // channel group (stage = channel group * N * tiles + unit); every rank of
   // a cluster runs the same number of stages.
   int v_begin, v_end;
-  int rank = 0, nranks = 1;
+  int rank = 0;
   if constexpr (LN) {
     rank = static_cast<int>(cluster_ctarank());
-    nranks = static_cast<int>(cluster_nctarank());
     const long long units = static_cast<long long>(a.N) * a.tiles;
     const long long cid = cluster_id_x(), ncl = nclusters_x();
     v_begin = static_cast<int>(rank * units + (units * cid) / ncl);
@@ -136,6 +136,7 @@ __global__ void __launch_bounds__(NhwcTileGeom::THREADS, sizeof(T) == 2 ? 2 : 1)
   int cur_cg = -1;
   float bias = 0.f;
   float ln_g = 1.f, ln_b = 0.f;  // LN: scale / shift of channel 32 cg + lane
+  int prev_n = 0, prev_tx = 0, prev_ty = 0;  // LN: the stage awaiting its store
 
   for (int v = v_begin, it = 0; v < v_end; ++v, ++it) {
     const int s = it & 1;
@@ -210,6 +211,12 @@ __global__ void __launch_bounds__(NhwcTileGeom::THREADS, sizeof(T) == 2 ? 2 : 1)
 
     // ---- + bias, round, into out[s] [y][x][lane]; TMA store -------------
     T* os = out_buf(s);
+    if constexpr (LN) {
+      // out[s] was last read by the store of stage it - 2, which the LN flow
+      // issues one iteration late; it is done before anyone writes out[s].
+      if (tid == 0) bulk_wait_read_all();
+      __syncthreads();
+    }
     const bool has_bias = bbase != nullptr;
 #pragma unroll
     for (int r = 0; r < R; ++r) {
@@ -222,8 +229,30 @@ __global__ void __launch_bounds__(NhwcTileGeom::THREADS, sizeof(T) == 2 ? 2 : 1)
       }
     }
     if constexpr (LN) {
-      ln_epilogue<T, LANES, TS * TS, G::THREADS>(os, reinterpret_cast<float*>(smem + M::OFF_LN), rank, nranks, a.C,
-                                                 a.ln.eps, a.ln.gamma != nullptr, ln_g, a.ln.beta != nullptr, ln_b);
+      // Deferred: finish stage it - 1 (its exchange ran behind this stage's
+      // FMAs), then publish this stage's partials.
+      const LnView<LANES, TS * TS> lv{reinterpret_cast<float*>(smem + M::OFF_LN)};
+      if (it > 0) {
+        cluster_wait();
+        ln_combine<LANES, TS * TS, G::THREADS>(lv, (it - 1) & 1, a.C, a.ln.eps);
+        __syncthreads();
+        ln_normalize<T, LANES, TS * TS, G::THREADS>(out_buf(s ^ 1), lv, cg * LANES, a.C, a.ln.gamma != nullptr,
+                                                    ln_g, a.ln.beta != nullptr, ln_b);
+        fence_proxy_async_smem();
+        __syncthreads();
+        if (tid == 0) {
+          tma_store_4d(&ymap, out_buf(s ^ 1), cg * LANES, prev_tx * TS, prev_ty * TS, prev_n);
+          bulk_commit();
+        }
+      } else {
+        __syncthreads();
+      }
+      ln_local_stats<T, LANES, TS * TS, G::THREADS>(os, lv, it & 1, cg * LANES, a.C);
+      cluster_arrive();
+      prev_n = n;
+      prev_tx = tx;
+      prev_ty = ty;
+      continue;
     }
     fence_proxy_async_smem();
     // The store that read out[s ^ 1] (issued one stage ago) is done before
@@ -235,7 +264,24 @@ __global__ void __launch_bounds__(NhwcTileGeom::THREADS, sizeof(T) == 2 ? 2 : 1)
       bulk_commit();
     }
   }
-  if constexpr (LN) cluster_sync();  // peers may still read this CTA's partial sums
+  if constexpr (LN) {
+    if (v_end > v_begin) {  // the last stage's deferred exchange
+      const LnView<LANES, TS * TS> lv{reinterpret_cast<float*>(smem + M::OFF_LN)};
+      const int last = (v_end - v_begin - 1) & 1;
+      cluster_wait();
+      ln_combine<LANES, TS * TS, G::THREADS>(lv, last, a.C, a.ln.eps);
+      __syncthreads();
+      ln_normalize<T, LANES, TS * TS, G::THREADS>(out_buf(last), lv, rank * LANES, a.C, a.ln.gamma != nullptr,
+                                                  ln_g, a.ln.beta != nullptr, ln_b);
+      fence_proxy_async_smem();
+      __syncthreads();
+      if (tid == 0) {
+        tma_store_4d(&ymap, out_buf(last), rank * LANES, prev_tx * TS, prev_ty * TS, prev_n);
+        bulk_commit();
+      }
+    }
+    cluster_sync();  // peers may still read this CTA's partial sums
+  }
   if (tid == 0) bulk_wait_all();
 }
 

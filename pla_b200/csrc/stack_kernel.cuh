@@ -34,7 +34,9 @@
 //  * LN (NHWC only): the stage's outputs go through the channel LayerNorm
 //    epilogue of ln_epilogue.cuh before the store.  The kernel then runs as
 //    clusters of C / LANES CTAs: rank r owns channel group r of the images
-//    the cluster visits, so its filters never change.
+//    the cluster visits, so its filters never change.  16-bit stages, which
+//    have the output ring, are normalised and stored one stage late, so the
+//    cluster exchange overlaps the next stage's FMAs.
 #pragma once
 
 #include "ln_epilogue.cuh"
@@ -199,10 +201,9 @@ __global__ void __launch_bounds__(StackGeom<S, kMixStack<T>>::THREADS, StackGeom
   // (virtual stage = channel group * N + image); every rank of a cluster
   // runs the same number of stages.
   int v_begin, v_end;
-  int rank = 0, nranks = 1;
+  int rank = 0;
   if constexpr (LN) {
     rank = static_cast<int>(cluster_ctarank());
-    nranks = static_cast<int>(cluster_nctarank());
     const long long cid = cluster_id_x(), ncl = nclusters_x();
     v_begin = rank * a.N + static_cast<int>((static_cast<long long>(a.N) * cid) / ncl);
     v_end = rank * a.N + static_cast<int>((static_cast<long long>(a.N) * (cid + 1)) / ncl);
@@ -218,7 +219,8 @@ __global__ void __launch_bounds__(StackGeom<S, kMixStack<T>>::THREADS, StackGeom
   uint32_t wh[(kTaps + 1) / 2];
   int cur_c = -1;
   float bias = 0.f;
-  float ln_g = 1.f, ln_b = 0.f;  // LN: this thread's channel scale / shift (step 5)
+  float ln_g = 1.f, ln_b = 0.f;  // LN: scale / shift of this thread's channel
+  int prev_img = 0;              // LN, 16-bit: image of the stage awaiting its store
 
   for (int v = v_begin, it = 0; v < v_end; ++v, ++it) {
     const int s = it & 1;
@@ -376,6 +378,12 @@ __global__ void __launch_bounds__(StackGeom<S, kMixStack<T>>::THREADS, StackGeom
     // ---- + bias, round, stage the output (fp32: in raw[s], whose input is
     // consumed; 16-bit: in out[s], whose last bulk store has been read) ----
     T* os = outb(s);
+    if constexpr (LN && MIX) {
+      // out[s] was last read by the store of stage it - 2, which the LN flow
+      // issues one iteration late; it is done before anyone writes out[s].
+      if (tid == 0) bulk_wait_read_all();
+      __syncthreads();
+    }
     const bool has_bias = bbase != nullptr;
 #pragma unroll
     for (int r = 0; r < R; ++r) {
@@ -393,10 +401,43 @@ __global__ void __launch_bounds__(StackGeom<S, kMixStack<T>>::THREADS, StackGeom
       }
     }
     if constexpr (LN) {
-      // In the epilogue thread t handles channel t % LANES: the same lane ln
+      // The epilogue's thread t handles channel t % LANES: the same lane ln
       // (THREADS = LANES x row groups), whose scale and shift it holds.
-      ln_epilogue<T, LANES, S * S, G::THREADS>(os, reinterpret_cast<float*>(smem + M::OFF_LN), rank, nranks, a.C,
-                                               a.ln.eps, a.ln.gamma != nullptr, ln_g, a.ln.beta != nullptr, ln_b);
+      const LnView<LANES, S * S> lv{reinterpret_cast<float*>(smem + M::OFF_LN)};
+      const int c0 = rank * LANES;
+      if constexpr (MIX) {
+        // Deferred: finish stage it - 1 (its exchange ran behind this
+        // stage's FMAs), then publish this stage's partials.
+        if (it > 0) {
+          cluster_wait();
+          ln_combine<LANES, S * S, G::THREADS>(lv, (it - 1) & 1, a.C, a.ln.eps);
+          __syncthreads();
+          ln_normalize<T, LANES, S * S, G::THREADS>(outb(s ^ 1), lv, c0, a.C, a.ln.gamma != nullptr, ln_g,
+                                                    a.ln.beta != nullptr, ln_b);
+          fence_proxy_async_smem();
+          __syncthreads();
+          if (tid == 0) {
+            tma_store_4d(&ymap, outb(s ^ 1), rank * LANES, 0, 0, prev_img);
+            bulk_commit();
+          }
+        } else {
+          __syncthreads();
+        }
+        ln_local_stats<T, LANES, S * S, G::THREADS>(os, lv, it & 1, c0, a.C);
+        cluster_arrive();
+        prev_img = n_img;
+        continue;
+      } else {
+        // fp32 stages are normalised in place (raw[s] is the next load's
+        // target), so the exchange is not deferred.
+        __syncthreads();
+        ln_local_stats<T, LANES, S * S, G::THREADS>(os, lv, it & 1, c0, a.C);
+        cluster_sync();
+        ln_combine<LANES, S * S, G::THREADS>(lv, it & 1, a.C, a.ln.eps);
+        __syncthreads();
+        ln_normalize<T, LANES, S * S, G::THREADS>(os, lv, c0, a.C, a.ln.gamma != nullptr, ln_g,
+                                                  a.ln.beta != nullptr, ln_b);
+      }
     }
     fence_proxy_async_smem();
     // 16-bit: before this barrier releases the next stage's writes into
@@ -419,7 +460,26 @@ __global__ void __launch_bounds__(StackGeom<S, kMixStack<T>>::THREADS, StackGeom
     }
     (void)lane_ok;
   }
-  if constexpr (LN) cluster_sync();  // peers may still read this CTA's partial sums
+  if constexpr (LN) {
+    if constexpr (MIX) {
+      if (v_end > v_begin) {  // the last stage's deferred exchange
+        const LnView<LANES, S * S> lv{reinterpret_cast<float*>(smem + M::OFF_LN)};
+        const int last = (v_end - v_begin - 1) & 1;
+        cluster_wait();
+        ln_combine<LANES, S * S, G::THREADS>(lv, last, a.C, a.ln.eps);
+        __syncthreads();
+        ln_normalize<T, LANES, S * S, G::THREADS>(outb(last), lv, rank * LANES, a.C, a.ln.gamma != nullptr, ln_g,
+                                                  a.ln.beta != nullptr, ln_b);
+        fence_proxy_async_smem();
+        __syncthreads();
+        if (tid == 0) {
+          tma_store_4d(&ymap, outb(last), rank * LANES, 0, 0, prev_img);
+          bulk_commit();
+        }
+      }
+    }
+    cluster_sync();  // peers may still read this CTA's partial sums
+  }
   if (tid == 0) bulk_wait_all();
 }
 
