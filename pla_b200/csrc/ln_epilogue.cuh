@@ -14,16 +14,17 @@
 //   ln_local_stats  each CTA reduces every (32-channel group, pixel) of its
 //                   stage on its own: sum s_g and, around the group mean
 //                   m_g = s_g / n_g, the sum of squared deviations q_g;
-//                   -> part[buf][g][p], part2[buf][g][p]; then the cluster
-//                   barrier is ARRIVED at (release);
+//                   -> s / m / q [buf][g][p]; then the cluster barrier is
+//                   ARRIVED at (release);
 //   ln_combine      after the barrier's WAIT (acquire), every CTA loads all
-//                   groups' (s_g, q_g) of its pixels from the owning ranks,
-//                   eight loads in flight at a time, and combines them in
-//                   group order: mean = sum s_g / C,
+//                   groups' (s_g, m_g, q_g) of its pixels from the owning
+//                   ranks, eight groups in flight at a time, and combines them
+//                   in group order: mean = sum s_g / C,
 //                   M = sum (q_g + n_g (m_g - mean)^2)  (Chan, Golub and
 //                   LeVeque's pairwise variance update: stable, one exchange),
 //                   inv = 1 / sqrt(M / C + eps);
-//   ln_normalize    z = ((v - mean) * inv) * gamma + beta, in place in os.
+//   ln_normalize    z = ((v - mean) * inv) * gamma + beta, in place in os,
+//                   16 bytes of channels per thread and step.
 //
 // Every operation is a correctly rounded fp32 add / multiply / divide /
 // square root in a fixed tree, which the CPU oracle's
@@ -34,7 +35,7 @@
 // Kernels with an output ring split the barrier around the next stage's
 // FMAs (arrive after stage i's local statistics, wait after stage i+1's
 // convolution), so the exchange's latency hides behind compute; stage i is
-// normalised and stored then.  part / part2 alternate between two buffers by
+// normalised and stored then.  The partials alternate between two buffers by
 // stage parity: a peer reads stage i's buffer between wait(i) and its own
 // arrive(i + 1), and the owner rewrites it at stage i + 2, after wait(i + 1).
 // The kernels end with one more cluster barrier so that no CTA exits while
@@ -96,23 +97,40 @@ __device__ __forceinline__ float dsmem_ld(uint32_t addr) {
   return v;
 }
 
-// Shared memory of the epilogue: part[2][GL][P], part2[2][GL][P] (two
-// buffers by stage parity), mean[P], inv[P].
+// Shared memory of the epilogue: sums s[2][GL][P], group means m[2][GL][P]
+// and squared deviations q[2][GL][P] (two buffers by stage parity), then
+// mean[P], inv[P], and the CTA's scales and shifts gamma[LANES], beta[LANES].
 template <int LANES, int P>
 struct LnSmem {
   static constexpr int GL = LANES / 32;
-  static constexpr uint32_t BYTES = static_cast<uint32_t>((4 * GL * P + 2 * P) * sizeof(float));
+  static constexpr uint32_t BYTES = static_cast<uint32_t>((6 * GL * P + 2 * P + 2 * LANES) * sizeof(float));
 };
 
 template <int LANES, int P>
 struct LnView {
   static constexpr int GL = LANES / 32;
   float* base;
-  __device__ float* part(int buf) const { return base + buf * GL * P; }
-  __device__ float* part2(int buf) const { return base + (2 + buf) * GL * P; }
-  __device__ float* mean() const { return base + 4 * GL * P; }
-  __device__ float* inv() const { return base + 4 * GL * P + P; }
+  __device__ float* part(int buf) const { return base + buf * GL * P; }         // s_g
+  __device__ float* part_m(int buf) const { return base + (2 + buf) * GL * P; }  // m_g
+  __device__ float* part2(int buf) const { return base + (4 + buf) * GL * P; }   // q_g
+  __device__ float* mean() const { return base + 6 * GL * P; }
+  __device__ float* inv() const { return base + 6 * GL * P + P; }
+  __device__ float* gamma() const { return base + 6 * GL * P + 2 * P; }
+  __device__ float* beta() const { return gamma() + LANES; }
 };
+
+// The CTA's LANES scales and shifts (channels c0 ...) as fp32 in shared
+// memory (1 / 0 for NULL vectors or channels past C).  Called once, before
+// the first stage; the stage barriers order it before any use.
+template <typename T, int LANES, int P, int THREADS>
+__device__ __forceinline__ void ln_load_affine(const LnView<LANES, P>& v, const void* gamma, const void* beta,
+                                               int c0, int C) {
+  for (int l = threadIdx.x; l < LANES; l += THREADS) {
+    const int c = c0 + l;
+    v.gamma()[l] = gamma && c < C ? to_acc(static_cast<const T*>(gamma)[c]) : 1.f;
+    v.beta()[l] = beta && c < C ? to_acc(static_cast<const T*>(beta)[c]) : 0.f;
+  }
+}
 
 // Channels of 32-channel group `gi` of this CTA's stage that exist (0..32).
 __device__ __forceinline__ int group_size(int C, int c0, int gi) {
@@ -120,12 +138,31 @@ __device__ __forceinline__ int group_size(int C, int c0, int gi) {
   return n < 0 ? 0 : (n > 32 ? 32 : n);
 }
 
-// (s_g, q_g) of every (group, pixel) of the stage in os -> part[buf], part2[buf].
+// (s_g, m_g, q_g) of `n` values, in ascending order from +0.
+template <bool FULL>
+__device__ __forceinline__ void group_stats(const float (&x)[32], int n, float& s, float& m, float& q2) {
+  s = 0.f;
+#pragma unroll
+  for (int j = 0; j < 32; ++j)
+    if (FULL || j < n) s = __fadd_rn(s, x[j]);
+  m = __fdiv_rn(s, static_cast<float>(FULL ? 32 : n));
+  q2 = 0.f;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    if (FULL || j < n) {
+      const float d = __fsub_rn(x[j], m);
+      q2 = __fadd_rn(q2, __fmul_rn(d, d));
+    }
+  }
+}
+
+// (s_g, m_g, q_g) of every (group, pixel) of the stage in os -> buffer `buf`.
 template <typename T, int LANES, int P, int THREADS>
 __device__ __forceinline__ void ln_local_stats(const T* os, const LnView<LANES, P>& v, int buf, int c0, int C) {
   constexpr int GL = LANES / 32;
   constexpr int VEC = 16 / sizeof(T);
   float* part = v.part(buf);
+  float* part_m = v.part_m(buf);
   float* part2 = v.part2(buf);
   for (int t = threadIdx.x; t < GL * P; t += THREADS) {
     const int gi = t / P, p = t - gi * P;
@@ -139,22 +176,13 @@ __device__ __forceinline__ void ln_local_stats(const T* os, const LnView<LANES, 
 #pragma unroll
       for (int j = 0; j < VEC; ++j) x[q * VEC + j] = to_acc(e[j]);
     }
-    float s = 0.f;
-#pragma unroll
-    for (int j = 0; j < 32; ++j)
-      if (j < n) s = __fadd_rn(s, x[j]);
-    float q2 = 0.f;
-    if (n > 0) {
-      const float m = __fdiv_rn(s, static_cast<float>(n));
-#pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        if (j < n) {
-          const float d = __fsub_rn(x[j], m);
-          q2 = __fadd_rn(q2, __fmul_rn(d, d));
-        }
-      }
-    }
+    float s = 0.f, m = 0.f, q2 = 0.f;
+    if (n == 32)
+      group_stats<true>(x, n, s, m, q2);
+    else if (n > 0)
+      group_stats<false>(x, n, s, m, q2);
     part[t] = s;
+    part_m[t] = m;
     part2[t] = q2;
   }
 }
@@ -167,7 +195,7 @@ __device__ __forceinline__ void ln_combine(const LnView<LANES, P>& v, int buf, i
   constexpr int CH = 8;  // remote loads in flight per thread
   const int ngroups = (C + 31) / 32;
   const float fc = static_cast<float>(C);
-  const uint32_t pa = smem_u32(v.part(buf)), qa = smem_u32(v.part2(buf));
+  const uint32_t pa = smem_u32(v.part(buf)), ma = smem_u32(v.part_m(buf)), qa = smem_u32(v.part2(buf));
   float* mean_s = v.mean();
   float* inv_s = v.inv();
   for (int p = threadIdx.x; p < P; p += THREADS) {
@@ -186,12 +214,12 @@ __device__ __forceinline__ void ln_combine(const LnView<LANES, P>& v, int buf, i
     const float mean = __fdiv_rn(s, fc);
     float m2 = 0.f;
     for (int g0 = 0; g0 < ngroups; g0 += CH) {
-      float sv[CH], qv[CH];
+      float mv[CH], qv[CH];
 #pragma unroll
       for (int j = 0; j < CH; ++j) {
         const int g = g0 + j;
         const uint32_t off = ((g % GL) * P + p) * 4u;
-        sv[j] = g < ngroups ? dsmem_ld(dsmem_map(pa + off, g / GL)) : 0.f;
+        mv[j] = g < ngroups ? dsmem_ld(dsmem_map(ma + off, g / GL)) : 0.f;
         qv[j] = g < ngroups ? dsmem_ld(dsmem_map(qa + off, g / GL)) : 0.f;
       }
 #pragma unroll
@@ -200,7 +228,7 @@ __device__ __forceinline__ void ln_combine(const LnView<LANES, P>& v, int buf, i
         if (g < ngroups) {
           const int n = C - g * 32 < 32 ? C - g * 32 : 32;
           const float fn = static_cast<float>(n);
-          const float e = __fsub_rn(__fdiv_rn(sv[j], fn), mean);
+          const float e = __fsub_rn(mv[j], mean);
           m2 = __fadd_rn(m2, __fadd_rn(qv[j], __fmul_rn(fn, __fmul_rn(e, e))));
         }
       }
@@ -210,22 +238,46 @@ __device__ __forceinline__ void ln_combine(const LnView<LANES, P>& v, int buf, i
   }
 }
 
-// z = ((v - mean) * inv) * gamma + beta in place.  Thread tid handles channel
-// c0 + tid % LANES (THREADS is a multiple of LANES), whose scale and shift it
-// holds in g / bt.
+// z = ((v - mean) * inv) * gamma + beta in place, one 16-byte chunk of
+// channels at a time.  Thread tid always handles chunk tid % NQ of a pixel
+// (THREADS is a multiple of NQ), channels c0 + VEC * (tid % NQ) + [0, VEC),
+// whose scales and shifts it reads from shared memory (ln_load_affine).
+// C * sizeof(T) is a multiple of 16 bytes, so a chunk is all in or all out.
+template <typename T, int LANES>
+struct LnChunk {
+  static constexpr int VEC = 16 / sizeof(T);
+  static constexpr int NQ = LANES / VEC;  // chunks per pixel
+};
+
 template <typename T, int LANES, int P, int THREADS>
 __device__ __forceinline__ void ln_normalize(T* os, const LnView<LANES, P>& v, int c0, int C, bool has_gamma,
-                                             float g, bool has_beta, float bt) {
-  static_assert(LANES % 32 == 0 && THREADS % LANES == 0, "fixed channel per thread");
+                                             bool has_beta) {
+  using K = LnChunk<T, LANES>;
+  static_assert(THREADS % K::NQ == 0, "fixed chunk per thread");
+  constexpr int PSTEP = THREADS / K::NQ;
   const float* mean_s = v.mean();
   const float* inv_s = v.inv();
-  if (c0 + static_cast<int>(threadIdx.x % LANES) >= C) return;
-  for (int i = threadIdx.x; i < P * LANES; i += THREADS) {
-    const int p = i / LANES;
-    float t = __fmul_rn(__fsub_rn(to_acc(os[i]), mean_s[p]), inv_s[p]);
-    if (has_gamma) t = __fmul_rn(t, g);
-    if (has_beta) t = __fadd_rn(t, bt);
-    os[i] = from_acc<T>(t);
+  const int q = threadIdx.x % K::NQ;
+  if (c0 + K::VEC * q >= C) return;
+  float g[K::VEC], bt[K::VEC];
+#pragma unroll
+  for (int j = 0; j < K::VEC; ++j) {
+    g[j] = v.gamma()[K::VEC * q + j];
+    bt[j] = v.beta()[K::VEC * q + j];
+  }
+  for (int p = threadIdx.x / K::NQ; p < P; p += PSTEP) {
+    uint4* cp = reinterpret_cast<uint4*>(os + p * LANES) + q;
+    uint4 u = *cp;
+    T* e = reinterpret_cast<T*>(&u);
+    const float mean = mean_s[p], inv = inv_s[p];
+#pragma unroll
+    for (int j = 0; j < K::VEC; ++j) {
+      float t = __fmul_rn(__fsub_rn(to_acc(e[j]), mean), inv);
+      if (has_gamma) t = __fmul_rn(t, g[j]);
+      if (has_beta) t = __fadd_rn(t, bt[j]);
+      e[j] = from_acc<T>(t);
+    }
+    *cp = u;
   }
 }
 

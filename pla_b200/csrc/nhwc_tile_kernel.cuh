@@ -135,7 +135,11 @@ __global__ void __launch_bounds__(NhwcTileGeom::THREADS, sizeof(T) == 2 ? 2 : 1)
   uint32_t wh[(kTaps + 1) / 2];
   int cur_cg = -1;
   float bias = 0.f;
-  float ln_g = 1.f, ln_b = 0.f;  // LN: scale / shift of channel 32 cg + lane
+  // LN: the CTA's scales and shifts (rank r always owns channel group r).
+  if constexpr (LN) {
+    const LnView<LANES, TS * TS> lv{reinterpret_cast<float*>(smem + M::OFF_LN)};
+    ln_load_affine<T, LANES, TS * TS, G::THREADS>(lv, a.ln.gamma, a.ln.beta, rank * LANES, a.C);
+  }
   int prev_n = 0, prev_tx = 0, prev_ty = 0;  // LN: the stage awaiting its store
 
   for (int v = v_begin, it = 0; v < v_end; ++v, ++it) {
@@ -155,10 +159,6 @@ __global__ void __launch_bounds__(NhwcTileGeom::THREADS, sizeof(T) == 2 ? 2 : 1)
         for (int t = 0; t < kTaps; ++t) wt[t] = to_acc(wbase[cw * kTaps + t]);
       }
       bias = bbase ? to_acc(bbase[cw]) : 0.f;
-      if constexpr (LN) {
-        if (a.ln.gamma) ln_g = to_acc(static_cast<const T*>(a.ln.gamma)[cw]);
-        if (a.ln.beta) ln_b = to_acc(static_cast<const T*>(a.ln.beta)[cw]);
-      }
     }
 
     mbar_wait_bounded(&bars[s], (it >> 1) & 1);
@@ -237,7 +237,7 @@ __global__ void __launch_bounds__(NhwcTileGeom::THREADS, sizeof(T) == 2 ? 2 : 1)
         ln_combine<LANES, TS * TS, G::THREADS>(lv, (it - 1) & 1, a.C, a.ln.eps);
         __syncthreads();
         ln_normalize<T, LANES, TS * TS, G::THREADS>(out_buf(s ^ 1), lv, cg * LANES, a.C, a.ln.gamma != nullptr,
-                                                    ln_g, a.ln.beta != nullptr, ln_b);
+                                                    a.ln.beta != nullptr);
         fence_proxy_async_smem();
         __syncthreads();
         if (tid == 0) {
@@ -272,7 +272,7 @@ __global__ void __launch_bounds__(NhwcTileGeom::THREADS, sizeof(T) == 2 ? 2 : 1)
       ln_combine<LANES, TS * TS, G::THREADS>(lv, last, a.C, a.ln.eps);
       __syncthreads();
       ln_normalize<T, LANES, TS * TS, G::THREADS>(out_buf(last), lv, rank * LANES, a.C, a.ln.gamma != nullptr,
-                                                  ln_g, a.ln.beta != nullptr, ln_b);
+                                                    a.ln.beta != nullptr);
       fence_proxy_async_smem();
       __syncthreads();
       if (tid == 0) {

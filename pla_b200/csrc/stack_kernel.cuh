@@ -146,8 +146,6 @@ __global__ void __launch_bounds__(StackGeom<S, kMixStack<T>>::THREADS, StackGeom
     stack_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap ymap,
                  const StackArgs a) {
   static_assert(!LN || NHWC, "the LayerNorm epilogue normalises the channels of NHWC pixels");
-  // The epilogue's thread t handles channel t % LANES, which must be lane ln.
-  static_assert(StackGeom<S, kMixStack<T>>::G == 1 || StackGeom<S, kMixStack<T>>::RG == 1, "ln == tid % LANES");
   constexpr bool MIX = kMixStack<T>;
   using G = StackGeom<S, MIX>;
   using M = StackSmem<T, S, LN>;
@@ -219,7 +217,11 @@ __global__ void __launch_bounds__(StackGeom<S, kMixStack<T>>::THREADS, StackGeom
   uint32_t wh[(kTaps + 1) / 2];
   int cur_c = -1;
   float bias = 0.f;
-  float ln_g = 1.f, ln_b = 0.f;  // LN: scale / shift of this thread's channel
+  // LN: the CTA's scales and shifts (rank r always owns channel group r).
+  if constexpr (LN) {
+    const LnView<LANES, S * S> lv{reinterpret_cast<float*>(smem + M::OFF_LN)};
+    ln_load_affine<T, LANES, S * S, G::THREADS>(lv, a.ln.gamma, a.ln.beta, rank * LANES, a.C);
+  }
   int prev_img = 0;              // LN, 16-bit: image of the stage awaiting its store
 
   for (int v = v_begin, it = 0; v < v_end; ++v, ++it) {
@@ -256,10 +258,6 @@ __global__ void __launch_bounds__(StackGeom<S, kMixStack<T>>::THREADS, StackGeom
         for (int t = 0; t < kTaps; ++t) wt[t] = to_acc(wbase[cw * kTaps + t]);
       }
       bias = bbase ? to_acc(bbase[cw]) : 0.f;
-      if constexpr (LN) {
-        if (a.ln.gamma) ln_g = to_acc(static_cast<const T*>(a.ln.gamma)[cw]);
-        if (a.ln.beta) ln_b = to_acc(static_cast<const T*>(a.ln.beta)[cw]);
-      }
     }
 
     // ---- raw stage in shared memory ------------------------------------
@@ -401,8 +399,6 @@ __global__ void __launch_bounds__(StackGeom<S, kMixStack<T>>::THREADS, StackGeom
       }
     }
     if constexpr (LN) {
-      // The epilogue's thread t handles channel t % LANES: the same lane ln
-      // (THREADS = LANES x row groups), whose scale and shift it holds.
       const LnView<LANES, S * S> lv{reinterpret_cast<float*>(smem + M::OFF_LN)};
       const int c0 = rank * LANES;
       if constexpr (MIX) {
@@ -412,8 +408,8 @@ __global__ void __launch_bounds__(StackGeom<S, kMixStack<T>>::THREADS, StackGeom
           cluster_wait();
           ln_combine<LANES, S * S, G::THREADS>(lv, (it - 1) & 1, a.C, a.ln.eps);
           __syncthreads();
-          ln_normalize<T, LANES, S * S, G::THREADS>(outb(s ^ 1), lv, c0, a.C, a.ln.gamma != nullptr, ln_g,
-                                                    a.ln.beta != nullptr, ln_b);
+          ln_normalize<T, LANES, S * S, G::THREADS>(outb(s ^ 1), lv, c0, a.C, a.ln.gamma != nullptr,
+                                                    a.ln.beta != nullptr);
           fence_proxy_async_smem();
           __syncthreads();
           if (tid == 0) {
@@ -435,8 +431,8 @@ __global__ void __launch_bounds__(StackGeom<S, kMixStack<T>>::THREADS, StackGeom
         cluster_sync();
         ln_combine<LANES, S * S, G::THREADS>(lv, it & 1, a.C, a.ln.eps);
         __syncthreads();
-        ln_normalize<T, LANES, S * S, G::THREADS>(os, lv, c0, a.C, a.ln.gamma != nullptr, ln_g,
-                                                  a.ln.beta != nullptr, ln_b);
+        ln_normalize<T, LANES, S * S, G::THREADS>(os, lv, c0, a.C, a.ln.gamma != nullptr,
+                                                    a.ln.beta != nullptr);
       }
     }
     fence_proxy_async_smem();
@@ -468,8 +464,8 @@ __global__ void __launch_bounds__(StackGeom<S, kMixStack<T>>::THREADS, StackGeom
         cluster_wait();
         ln_combine<LANES, S * S, G::THREADS>(lv, last, a.C, a.ln.eps);
         __syncthreads();
-        ln_normalize<T, LANES, S * S, G::THREADS>(outb(last), lv, rank * LANES, a.C, a.ln.gamma != nullptr, ln_g,
-                                                  a.ln.beta != nullptr, ln_b);
+        ln_normalize<T, LANES, S * S, G::THREADS>(outb(last), lv, rank * LANES, a.C, a.ln.gamma != nullptr,
+                                                    a.ln.beta != nullptr);
         fence_proxy_async_smem();
         __syncthreads();
         if (tid == 0) {
