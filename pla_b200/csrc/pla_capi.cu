@@ -14,6 +14,7 @@
 #include "cm_kernel.cuh"
 #include "generic_kernel.cuh"
 #include "nhwc_tile_kernel.cuh"
+#include "pair_kernel.cuh"
 #include "pla_common.cuh"
 #include "stack_kernel.cuh"
 #include "tile_kernel.cuh"
@@ -142,9 +143,10 @@ CUtensorMapDataType tmap_dtype(int dtype) {
 }
 
 // Stack of `planes` planes of `rows` x `width` elements; strides in elements.
+// The box is G::PITCH x G::ROWS x box_planes.
 template <typename T, typename G>
 int make_tile_map(CUtensorMap* map, const void* x, int dtype, int width, int rows, int planes,
-                  long long row_stride, long long plane_stride) {
+                  long long row_stride, long long plane_stride, int box_planes = 1) {
   PFN_cuTensorMapEncodeTiled_v12000 enc;
   int st = encoder(&enc);
   if (st != PLA_OK) return st;
@@ -152,7 +154,8 @@ int make_tile_map(CUtensorMap* map, const void* x, int dtype, int width, int row
                               static_cast<cuuint64_t>(planes)};
   const cuuint64_t strides[2] = {static_cast<cuuint64_t>(row_stride) * sizeof(T),
                                  static_cast<cuuint64_t>(plane_stride) * sizeof(T)};
-  const cuuint32_t box[3] = {static_cast<cuuint32_t>(G::PITCH), static_cast<cuuint32_t>(G::ROWS), 1};
+  const cuuint32_t box[3] = {static_cast<cuuint32_t>(G::PITCH), static_cast<cuuint32_t>(G::ROWS),
+                             static_cast<cuuint32_t>(box_planes)};
   const cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = enc(map, tmap_dtype(dtype), 3, const_cast<void*>(x), dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -304,6 +307,45 @@ int launch_tile_dtype(int dtype, const void* x, const void* w, const void* b, co
 
 // One fused band step with the halo exchange over peer memory (wide tiles,
 // host taps, one plane).  `links` carries the peer pointers and flags.
+// NCHW stacks of 56 x 56 16-bit planes (pair_kernel.cuh).  Below a few
+// stages per SM the plane-tile kernel's shorter tiles fill the GPU better.
+bool pair_path_ok(const void* x, const void* y, int dtype, long long n, long long c, int h, int w, int sms) {
+  if (dtype != PLA_BF16 && dtype != PLA_F16) return false;
+  if (h != 56 || w != 56) return false;
+  if (!aligned(x, 16) || !aligned(y, 16)) return false;
+  const long long planes = n * c;
+  return planes <= 0x7fffffffll && planes >= 8ll * sms;
+}
+
+template <typename T>
+int launch_pair(const void* x, const void* w, const void* b, void* y, int dtype, int n, int c,
+                cudaStream_t stream) {
+  using G = PairGeom<T>;
+  int st;
+  DeviceInfo* d = device_info(&st);
+  if (!d) return st;
+  PairArgs a;
+  a.w = w; a.b = b; a.y = y;
+  a.N = n; a.C = c;
+  a.planes = n * c;  // < 2^31 (pair_path_ok)
+  a.stages = (a.planes + 1) / 2;
+  a.cp_major = (c % 2 == 0) ? 1 : 0;
+  a.div_n = make_fastdiv(n);
+  a.div_c = make_fastdiv(c);
+  constexpr long long kPlane = static_cast<long long>(G::S) * G::S;
+  CUtensorMap map;
+  st = make_tile_map<T, G>(&map, x, dtype, G::S, G::S, a.planes, G::S, kPlane, G::PL);
+  if (st != PLA_OK) return st;
+  int per_sm = 1;
+  st = kernel_setup<pair_kernel<T>>(G::THREADS, G::SMEM, &per_sm);
+  if (st != PLA_OK) return st;
+  const long long slots = static_cast<long long>(d->sms) * per_sm;
+  const int grid = static_cast<int>(a.stages < slots ? a.stages : slots);
+  pair_kernel<T><<<grid, G::THREADS, G::SMEM, stream>>>(map, a);
+  PLA_CUDA(cudaGetLastError());
+  return PLA_OK;
+}
+
 template <typename T>
 int launch_tile_halo(const void* in, const HostTaps& ht, void* out_rows, int dtype, int rows, int width,
                      HaloLinks links, cudaStream_t stream) {
@@ -930,6 +972,14 @@ int pla_depthwise7x7_forward(const void* x, const void* w, const void* b, void* 
   if (dtype != PLA_F64) {
     if (stack_path_ok(x, y, dtype, layout, n, c, h, width))
       return launch_stack_dtype(dtype, layout == PLA_NHWC, x, w, b, y, n, c, h, s);
+    if (layout == PLA_NCHW && dtype != PLA_F32) {
+      int st;
+      DeviceInfo* d = device_info(&st);
+      if (!d) return st;
+      if (pair_path_ok(x, y, dtype, n, c, h, width, d->sms))
+        return dtype == PLA_BF16 ? launch_pair<__nv_bfloat16>(x, w, b, y, dtype, n, c, s)
+                                 : launch_pair<__half>(x, w, b, y, dtype, n, c, s);
+    }
     if (layout == PLA_NCHW && (width >= 64 || use_narrow_tiles(width, h)) && planes <= 0x7fffffffll &&
         tile_path_ok(x, y, dtype, width, width, plane, static_cast<int>(planes))) {
       return launch_tile_dtype(dtype, x, w, b, nullptr, y, static_cast<int>(planes), c, h, width, width, plane, 0,

@@ -518,3 +518,21 @@ def test_nhwc_spatial_tiles_match_oracle(shape, dtype, bias):
     y = depthwise7x7(x.to(DEV), w.to(DEV), None if b is None else b.to(DEV))
     assert y.is_contiguous(memory_format=torch.channels_last)
     _assert_equal(y, oracle.depthwise7x7(x, w, b))
+
+
+@pytest.mark.parametrize("shape,dtype,bias", [
+    ((16, 96, 56, 56), torch.bfloat16, True),   # C even: stages walk channel pairs
+    ((13, 97, 56, 56), torch.bfloat16, True),   # C odd, odd plane count: last stage half past the end
+    ((12, 100, 56, 56), torch.float16, False),
+    ((3, 5, 56, 56), torch.bfloat16, True),     # too few planes: the plane-tile kernel instead
+])
+def test_plane_pair_path_matches_oracle(shape, dtype, bias):
+    """Large NCHW stacks of 56 x 56 16-bit planes run two planes per stage
+    (224 threads, no column past the plane edge); output == oracle bit for bit,
+    no device fault recorded."""
+    from pla_b200 import depthwise7x7
+
+    x, w, b = _dw_inputs(500 + shape[1], shape, dtype, bias)
+    y = depthwise7x7(x.to(DEV), w.to(DEV), None if b is None else b.to(DEV))
+    _assert_equal(y, oracle.depthwise7x7(x, w, b))
+    assert _lib_faults() == 0
