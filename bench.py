@@ -26,7 +26,10 @@ one JSON line.  Workloads (the benchmark configurations; synthetic seeded inputs
 
 A "step" is one pass of the hot path over one batch of input already resident
 in HBM; consecutive steps rotate over enough buffer sets that every step's
-inputs are out of L2 (footprint > 2 x 126 MB).  `value` is whole-job
+inputs are out of L2 (footprint > 2 x 126 MB).  The K timed steps are captured
+as one CUDA graph and replayed once (stream launches with --no-graph; always
+for the multi-GPU iterated stencil); the line also gives the stream-launch
+time of the same K steps (`stream_ms_per_step`).  `value` is whole-job
 compulsory bytes (input + output + weights + bias) / device time (CUDA events,
 max over ranks).  `e2e` repeats the measurement through the public API with
 pinned host buffers, host<->device copies inside the timed region.
@@ -223,6 +226,12 @@ class StencilCfg2:
         if st:
             raise RuntimeError(f"pla_stencil7x7_forward_taps failed: {st}")
 
+    graph_ok = True  # a step is one plain launch on the bound stream
+
+    def rebind(self, stream_ptr):
+        """Launch the bound calls on another stream (the CUDA-graph capture stream)."""
+        self._args = [a[:-1] + (stream_ptr,) for a in self._args]
+
     # end-to-end through the public module API, pinned host buffers
     def e2e_setup(self):
         self.hx = [self.x_cpu.clone().pin_memory() for _ in range(2)]
@@ -354,6 +363,12 @@ class DepthwiseBase:
     @staticmethod
     def batch_slice(N, world, rank):
         return slice(0, N)
+
+    graph_ok = True  # a step is one plain launch per stage on the bound stream
+
+    def rebind(self, stream_ptr):
+        """Launch the bound calls on another stream (the CUDA-graph capture stream)."""
+        self._args = [[a[:-1] + (stream_ptr,) for a in per] for per in self._args]
 
     _stage_events = None
 
@@ -782,6 +797,7 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=20)
     ap.add_argument("--cpu-budget", type=float, default=15.0, help="seconds of CPU work for cpu_baseline")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-graph", action="store_true", help="time the K steps as stream launches, no CUDA graph")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -802,37 +818,76 @@ def main():
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
 
     wl = Wl(rank, world, dev)
-    stream = torch.cuda.current_stream(dev)
+    # Workloads whose step is one plain launch per stage run their K timed
+    # steps as one CUDA graph (captured once, replayed once): the graph holds
+    # exactly those K steps' launches with the same bound arguments, and the
+    # host's per-launch submission drops out of the device timeline.
+    # --no-graph times the K steps as stream launches instead.  The multi-GPU
+    # iterated stencil (halo exchange) always runs as stream launches.
+    use_graph = getattr(wl, "graph_ok", False) and not args.no_graph
+    if use_graph:
+        stream = torch.cuda.Stream(dev)
+        wl.rebind(stream.cuda_stream)
+        torch.cuda.set_stream(stream)
+    else:
+        stream = torch.cuda.current_stream(dev)
 
     def barrier():
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize(dev)
 
-    for i in range(args.warmup):
-        wl.step(i)
+    def run_steps(first, n):
+        for i in range(n):
+            wl.step(first + i)
+
+    run_steps(0, args.warmup)
     barrier()
 
     K = args.steps
     # One event pair around the K steps: events between steps would add
     # their own gaps to the kernels they bracket.  Steps of several launches
     # (the ConvNeXt sweep) also bracket their dominant launch, for the
-    # roofline of that kernel.
+    # roofline of that kernel (in stream mode: in the timed loop; in graph
+    # mode: in the stream-mode pass after it).
     multi = getattr(wl, "launches_per_step", 1) > 1 and hasattr(wl, "arm_stage_timing")
-    if multi:
+    graph = None
+    if use_graph:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            run_steps(args.warmup, K)
+        # One untimed replay: the GPU idled through the capture.
+        graph.replay()
+        barrier()
+    elif multi:
         wl.arm_stage_timing(K)
     e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(dev) as clk:
         barrier()
         t_wall = time.perf_counter()
         e_start.record(stream)
-        for i in range(K):
-            wl.step(args.warmup + i)
+        if graph is not None:
+            graph.replay()
+        else:
+            run_steps(args.warmup, K)
         e_end.record(stream)
         barrier()
         t_wall = time.perf_counter() - t_wall
     total_ms = e_start.elapsed_time(e_end)
     mean_step_ms = total_ms / K
+    stream_ms_per_step = None
+    if graph is not None:
+        del graph
+        # The same K steps as stream launches, for comparison (this rank).
+        if multi:
+            wl.arm_stage_timing(K)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        e0.record(stream)
+        run_steps(args.warmup, K)
+        e1.record(stream)
+        barrier()
+        stream_ms_per_step = e0.elapsed_time(e1) / K
     dom_ms = wl.stage_ms() if multi else None
     t = torch.tensor([total_ms, float(wl.bytes), float(wl.points)], dtype=torch.float64, device=dev)
     if world > 1:
@@ -930,6 +985,8 @@ def main():
                          "fma_frac": (job_points / world) / (mean_step_ms * 1e-3) / 1e9 / fma_gpts},
             "cpu_baseline": cpu_baseline, "e2e": e2e, **({"unfused_pair": unfused} if unfused else {}),
             "gpu_launches": K * wl.launches_per_step, "clocks": clocks,
+            "launch_mode": "one CUDA graph of the K steps, replayed once" if use_graph else "stream launches",
+            **({"stream_ms_per_step": stream_ms_per_step} if stream_ms_per_step is not None else {}),
             "wall_s_timed_region": t_wall,
         }
         print(json.dumps(line), flush=True)
