@@ -67,7 +67,7 @@ __device__ __forceinline__ int pair_first_plane(int v, const PairArgs& a) {
 }
 
 template <typename T>
-__global__ void __launch_bounds__(PairGeom<T>::THREADS, 3)
+__global__ void __launch_bounds__(PairGeom<T>::THREADS, 4)
     pair_kernel(const __grid_constant__ CUtensorMap tmap, const PairArgs a) {
   using G = PairGeom<T>;
   constexpr int NT = kTaps;
