@@ -854,7 +854,9 @@ def main():
     graph = None
     if use_graph:
         graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph, stream=stream):
+        # thread_local: the process group's watchdog thread may query its
+        # (completed) events while this thread captures.
+        with torch.cuda.graph(graph, stream=stream, capture_error_mode="thread_local"):
             run_steps(args.warmup, K)
         # One untimed replay: the GPU idled through the capture.
         graph.replay()
