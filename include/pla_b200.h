@@ -87,7 +87,9 @@ PLA_API int pla_version(void);
  * with the argument meaning of launch_direct: x may be strided
  * (element strides sn, sh, sw; sn ignored when n == 1), y is contiguous
  * [n, h, width], w holds 49 taps row-major, b is NULL or one element, all of
- * dtype `dtype` (enum pla_dtype).  Unlike the reference it returns a status.
+ * dtype `dtype` (enum pla_dtype).  y must not overlap x (as with the
+ * reference, whose extension allocates a fresh output).  Unlike the
+ * reference it returns a status.
  */
 PLA_API int pla_stencil7x7_forward(const void* x, const void* w, const void* b, void* y,
                            int n, int h, int width,
@@ -120,7 +122,7 @@ PLA_API int pla_stencil7x7_forward_taps(const void* x, const float* taps, const 
  *    model_cutlass_autotune_v5.py:403-420).
  * Differences: w is the module's own [C,1,7,7] weight (no [C,8,80] repack),
  * b may be non-NULL ([C]), dtype may be f32/bf16/f16/f64 and layout NCHW or
- * NHWC.  x and y are dense in `layout`.
+ * NHWC.  x and y are dense in `layout` and must not overlap.
  */
 PLA_API int pla_depthwise7x7_forward(const void* x, const void* w, const void* b, void* y,
                              int n, int c, int h, int width,

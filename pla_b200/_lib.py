@@ -92,6 +92,30 @@ def ptr(t: torch.Tensor | None):
     return None if t is None else t.data_ptr()
 
 
+def overlaps(a: torch.Tensor, b: torch.Tensor) -> bool:
+    """Whether the memory spans of two CUDA tensors intersect.
+
+    The single-step kernels read each input halo after other CTAs may have
+    stored their outputs, so an output that overlaps its input would give
+    wrong results; the ops reject it instead.
+    """
+    if a.numel() == 0 or b.numel() == 0 or a.device != b.device:
+        return False
+
+    def span(t):
+        lo = hi = t.data_ptr()
+        for size, stride in zip(t.shape, t.stride()):
+            ext = (size - 1) * stride * t.element_size()
+            if ext < 0:
+                lo += ext
+            else:
+                hi += ext
+        return lo, hi + t.element_size()
+
+    (a0, a1), (b0, b1) = span(a), span(b)
+    return a0 < b1 and b0 < a1
+
+
 class HostTaps:
     """A 7x7 filter (+ optional bias) copied to host fp32 memory for the *_taps entry points.
 

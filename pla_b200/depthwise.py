@@ -80,6 +80,8 @@ def depthwise_kxk(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | No
         out = torch.empty(x.shape, dtype=x.dtype, device=x.device, memory_format=fmt)
     elif out.shape != x.shape or not out.is_contiguous(memory_format=fmt) or out.dtype != x.dtype:
         raise RuntimeError("out must match x's shape, dtype and memory format")
+    elif _lib.overlaps(out, x):
+        raise RuntimeError("out must not overlap x")
     if out.numel() == 0:
         return out
     weight = weight.detach().contiguous()
@@ -124,6 +126,8 @@ def depthwise7x7_layernorm(x: torch.Tensor, weight: torch.Tensor, bias: torch.Te
         out = torch.empty(x.shape, dtype=x.dtype, device=x.device, memory_format=torch.channels_last)
     elif out.shape != x.shape or not out.is_contiguous(memory_format=torch.channels_last) or out.dtype != x.dtype:
         raise RuntimeError("out must match x's shape, dtype and channels_last format")
+    elif _lib.overlaps(out, x):
+        raise RuntimeError("out must not overlap x")
     if out.numel() == 0:
         return out
     vecs = [None if t is None else t.detach().contiguous() for t in (bias, norm_weight, norm_bias)]

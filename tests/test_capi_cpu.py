@@ -149,3 +149,20 @@ def test_depthwise_layernorm_module_interface():
     assert tuple(m.dwconv.weight.shape) == (96, 1, 7, 7) and m.norm.eps == 1e-6
     with pytest.raises(ValueError):
         m(torch.rand(1, 96, 7, 7).contiguous(memory_format=torch.channels_last))
+
+
+def test_overlap_check_spans():
+    """The ops' out/x overlap guard works on memory spans (CPU tensors stand in for the addresses)."""
+    import torch
+
+    from pla_b200 import _lib
+
+    base = torch.zeros(4, 8, 16, 16)
+    assert _lib.overlaps(base, base)
+    assert _lib.overlaps(base[1:3], base[2:4])
+    assert not _lib.overlaps(base[0:2], base[2:4])
+    assert _lib.overlaps(base.permute(0, 2, 3, 1), base[3])
+    assert not _lib.overlaps(base[:, :, :, :8][0], base[1])
+    other = torch.zeros(4, 8, 16, 16)
+    assert not _lib.overlaps(base, other)
+    assert not _lib.overlaps(base[:0], base)

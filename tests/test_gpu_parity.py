@@ -536,3 +536,17 @@ def test_plane_pair_path_matches_oracle(shape, dtype, bias):
     y = depthwise7x7(x.to(DEV), w.to(DEV), None if b is None else b.to(DEV))
     _assert_equal(y, oracle.depthwise7x7(x, w, b))
     assert _lib_faults() == 0
+
+
+def test_outputs_overlapping_the_input_are_rejected():
+    """Single-step ops read input halos that other CTAs may already have
+    overwritten, so an output overlapping the input is refused before launch."""
+    from pla_b200 import depthwise7x7, stencil7x7
+
+    x = torch.randn(2, 64, 14, 14, device=DEV)
+    w = torch.randn(64, 1, 7, 7, device=DEV)
+    with pytest.raises(RuntimeError, match="overlap"):
+        depthwise7x7(x, w, None, out=x)
+    g = torch.rand(1, 1, 64, 128, device=DEV)
+    with pytest.raises(RuntimeError, match="overlap"):
+        stencil7x7(g, torch.rand(1, 1, 7, 7, device=DEV), None, out=g)
