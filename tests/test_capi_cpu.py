@@ -166,3 +166,26 @@ def test_overlap_check_spans():
     other = torch.zeros(4, 8, 16, 16)
     assert not _lib.overlaps(base, other)
     assert not _lib.overlaps(base[:0], base)
+
+
+def test_bench_reference_arm_line_on_cpu():
+    """`bench.py --impl reference` (the reference's CPU path) prints one JSON
+    line with the contract's keys; it needs no GPU."""
+    import json
+    import subprocess
+    import sys
+
+    r = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference", "--steps", "2",
+                        "--warmup", "1", "--workload", "dw_cfg1"], capture_output=True, text=True, timeout=300,
+                       cwd=ROOT)
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = [ln for ln in r.stdout.splitlines() if ln.startswith("{")]
+    assert len(lines) == 1
+    d = json.loads(lines[0])
+    assert d["impl"] == "reference" and d["steps"] == 2 and d["warmup"] >= 3
+    for key in ("metric", "value", "unit", "n_gpus", "ms_per_step", "higher_is_better", "scaling", "dtype",
+                "config", "cpu_baseline", "e2e"):
+        assert key in d, key
+    assert d["value"] > 0 and d["cpu_baseline"]["value"] == d["value"]
+    assert d["e2e"] == {"value": d["value"], "unit": d["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+    assert d["config"]["workload"] == "depthwise7x7_cfg1_1x96x56x56_f32"
