@@ -1,0 +1,87 @@
+"""Structural checks of the plane-pair kernel's thread geometry, on the CPU.
+
+pla_b200/csrc/pair_kernel.cuh maps 224 threads onto a stage of two 56 x 56
+planes held in shared memory as a 72 x 62 x 2 TMA box (x from -8, y from -3).
+These tests restate that mapping and check, without a GPU, that every output
+of the stage is owned by exactly one thread, that every shared-memory load
+stays inside the box and is 8-byte aligned, that the element a tap reads is
+the input the 7x7 correlation needs, and that a half-warp's 64-bit loads hit
+distinct banks.  They follow the structural tests of the reference's stencil
+kernels (tile coverage and alignment, data/stencil_cuda_v2/test_stencil.py:8-66).
+"""
+import itertools
+
+# PairGeom<bf16> (pla_b200/csrc/pair_kernel.cuh)
+S, PL, R, ELEM = 56, 2, 7, 2
+RG, CG = S // R, S // 4
+THREADS = PL * RG * CG
+LEFT = 16 // ELEM
+PITCH, ROWS = S + 2 * LEFT, S + 6
+
+
+def thread_map(tid):
+    pl = tid // (RG * CG)
+    rem = tid - pl * RG * CG
+    rg = rem // CG
+    return pl, rg, rem - rg * CG
+
+
+def load_offsets(tid):
+    """Element offsets of the thread's three 64-bit loads for each of its 13 input rows."""
+    pl, rg, cg = thread_map(tid)
+    base = pl * ROWS * PITCH + (rg * R) * PITCH + 4 * cg + (LEFT - 4)
+    return [[base + ir * PITCH + q for q in (0, 4, 8)] for ir in range(R + 6)]
+
+
+def test_threads_and_box_shape():
+    assert THREADS == 224 and THREADS % 32 == 0
+    assert (PITCH * ELEM) % 16 == 0 and (LEFT * ELEM) % 16 == 0  # TMA box width and x start
+    assert LEFT >= 4  # the thread's window starts 4 columns left of its first output
+
+
+def test_every_output_owned_once():
+    owners = {}
+    for tid in range(THREADS):
+        pl, rg, cg = thread_map(tid)
+        for r, j in itertools.product(range(R), range(4)):
+            key = (pl, rg * R + r, 4 * cg + j)
+            assert key not in owners
+            owners[key] = tid
+    assert len(owners) == PL * S * S
+
+
+def test_loads_inside_box_and_aligned():
+    box = PL * ROWS * PITCH
+    for tid in range(THREADS):
+        for row in load_offsets(tid):
+            for off in row:
+                assert 0 <= off and off + 4 <= box
+                assert (off * ELEM) % 8 == 0
+
+
+def test_taps_read_the_correlation_inputs():
+    """u[k / 2] half k & 1 is input column 4 cg - 4 + k of box row rg * 7 + ir;
+    output (r, j) with tap (ky, kx) uses ir = r + ky and k = j + kx + 1."""
+    for tid in range(THREADS):
+        pl, rg, cg = thread_map(tid)
+        base = pl * ROWS * PITCH + (rg * R) * PITCH + 4 * cg + (LEFT - 4)
+        for r, j, ky, kx in itertools.product(range(R), range(4), range(7), range(7)):
+            ir, k = r + ky, j + kx + 1
+            assert 0 <= k < 12
+            off = base + ir * PITCH + k - pl * ROWS * PITCH
+            box_row, box_col = divmod(off, PITCH)
+            in_row, in_col = box_row - 3, box_col - LEFT
+            assert (in_row, in_col) == (rg * R + r + ky - 3, 4 * cg + j + kx - 3)
+
+
+def test_half_warp_loads_hit_distinct_banks():
+    for warp in range(THREADS // 32):
+        for half in (0, 1):
+            lanes = range(warp * 32 + 16 * half, warp * 32 + 16 * half + 16)
+            for ir in range(R + 6):
+                for q in range(3):
+                    banks = []
+                    for tid in lanes:
+                        word = load_offsets(tid)[ir][q] * ELEM // 4
+                        banks += [word % 32, (word + 1) % 32]
+                    assert len(set(banks)) == len(banks), (warp, half, ir, q)
