@@ -85,3 +85,19 @@ def test_half_warp_loads_hit_distinct_banks():
                         word = load_offsets(tid)[ir][q] * ELEM // 4
                         banks += [word % 32, (word + 1) % 32]
                     assert len(set(banks)) == len(banks), (warp, half, ir, q)
+
+
+def test_tma_x_coordinates_stay_16_byte_aligned():
+    """Every tiled TMA load of the plane kernels starts its innermost
+    coordinate on a 16-byte boundary (an unaligned x is an illegal instruction
+    on sm_100): plane tiles at x = tx * TW - LEFT (TileGeom, tile_kernel.cuh)
+    for every element size and tile shape, and plane-pair stages at x = -LEFT."""
+    for elem in (4, 2):
+        left = 16 // elem
+        for lx in (32, 16):            # (R, LX) = (8, 32), (7, 16), (2, 16)
+            tw = 4 * lx
+            pitch = tw + 2 * left
+            assert (pitch * elem) % 16 == 0
+            for tx in range(64):
+                assert ((tx * tw - left) * elem) % 16 == 0
+    assert (-LEFT * ELEM) % 16 == 0
