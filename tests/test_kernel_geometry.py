@@ -101,3 +101,37 @@ def test_tma_x_coordinates_stay_16_byte_aligned():
             for tx in range(64):
                 assert ((tx * tw - left) * elem) % 16 == 0
     assert (-LEFT * ELEM) % 16 == 0
+
+
+def _stack_geom(s, mix):
+    """StackGeom<S, MIX> (pla_b200/csrc/stack_kernel.cuh)."""
+    r = 7 if s == 7 else 2
+    rg = (s + r - 1) // r
+    g = 4 if s == 7 else 1
+    return r, rg, g, 32 * g
+
+
+def test_stack_kernel_rows_lanes_and_stage_copies():
+    """Plane-stack kernel: the (row group, row) pairs of a plane cover its S
+    rows once, the lanes cover the stage's LANES planes once, every raw-stage
+    read is inside the stage, 16-bit NCHW rows of even S are read as aligned
+    32-bit words, and a stage is a whole number of 16-byte bulk-copy units."""
+    for s in (7, 14, 28):
+        for elem in (4, 2):
+            mix = elem == 2
+            r, rg, g, lanes = _stack_geom(s, mix)
+            rows = [grp * r + i for grp in range(rg) for i in range(r) if grp * r + i < s]
+            assert sorted(rows) == list(range(s))
+            warps = rg * g
+            lane_ids = sorted({(w // rg) * 32 + l for w in range(warps) for l in range(32)})
+            assert lane_ids == list(range(lanes))
+            plane = s * s
+            stage_elems = lanes * plane
+            assert (stage_elems * elem) % 16 == 0
+            for ln in range(lanes):
+                for iy in range(s):
+                    first, last = ln * plane + iy * s, ln * plane + iy * s + s - 1   # NCHW row
+                    assert 0 <= first and last < stage_elems
+                    if mix and s % 2 == 0:
+                        assert (first * elem) % 4 == 0
+                    assert (iy * s + s - 1) * lanes + ln < stage_elems                 # NHWC row
