@@ -135,3 +135,38 @@ def test_stack_kernel_rows_lanes_and_stage_copies():
                     if mix and s % 2 == 0:
                         assert (first * elem) % 4 == 0
                     assert (iy * s + s - 1) * lanes + ln < stage_elems                 # NHWC row
+
+
+def test_tile_kernel_covers_planes_and_reads_inside_the_box():
+    """Plane-tile kernel (TileGeom, tile_kernel.cuh): for each tile shape and
+    filter side, the stored outputs of all tiles cover a W x H plane once, and
+    every tap of a thread reads inside the TMA box, at the input element the
+    correlation needs (box x from tx * TW - LEFT, y from ty * TH - K / 2)."""
+    threads = 128
+    for elem in (4, 2):
+        left = 16 // elem
+        for r, lx in ((8, 32), (7, 16), (2, 16)):
+            tw, th = 4 * lx, (threads // 32) * (32 // lx) * r
+            pitch = tw + 2 * left
+            for k in (3, 5, 7):
+                rows = th + k - 1
+                cx = 4 - k // 2
+                for (h, w) in ((th, tw), (th + 5, tw + 12), (3, 8)):
+                    tiles_x, tiles_y = -(-w // tw), -(-h // th)
+                    seen = set()
+                    for ty, tx, tid in itertools.product(range(tiles_y), range(tiles_x), range(threads)):
+                        warp, lane = divmod(tid, 32)
+                        rgrp, cgrp = warp * (32 // lx) + lane // lx, lane % lx
+                        for rr, j in itertools.product(range(r), range(4)):
+                            oy, ox = ty * th + rgrp * r + rr, tx * tw + 4 * cgrp + j
+                            if oy < h and ox < w:
+                                assert (oy, ox) not in seen
+                                seen.add((oy, ox))
+                            for ky, kx in ((0, 0), (k - 1, k - 1), (k // 2, 0), (0, k - 1)):
+                                ir, col = rr + ky, j + kx + cx
+                                assert 0 <= col < 12
+                                box_row, box_col = rgrp * r + ir, 4 * cgrp + left - 4 + col
+                                assert box_row < rows and box_col < pitch
+                                assert (ty * th - k // 2 + box_row, tx * tw - left + box_col) == \
+                                    (oy + ky - k // 2, ox + kx - k // 2)
+                    assert len(seen) == h * w
