@@ -8,15 +8,19 @@ depthwise hot path on 1..8 B200s, with the reference's CPU path beside it.
 N > 1 is launched one process per GPU by torch.distributed.run.  Rank 0 prints
 one JSON line.  Workloads (the benchmark configurations; synthetic seeded inputs):
 
-  stencil_cfg2   (default) single-step 7x7 stencil, fp32 1x1x4096x4096, seed 1;
+  iterate_cfg5   (default) one Jacobi step of the 32768^2 fp32 iterated stencil
+                 (seed 4), row bands over the GPUs with a 3-row halo exchange
+                 fused into the step kernel (strong scaling); e2e = the whole
+                 100-step job with the band copied in and out; after timing,
+                 rows of every band are checked bit for bit against the CPU
+                 oracle ("parity" in the line; exit 3 on a mismatch)
+  stencil_cfg2   single-step 7x7 stencil, fp32 1x1x4096x4096, seed 1;
                  one grid per GPU (weak scaling, no collective)
   dw_cfg1        depthwise fp32 1x96x56x56 + bias, seed 0
   dw_cfg3_nchw   depthwise bf16 128x384x14x14 + bias, NCHW, seed 2
   dw_cfg3_nhwc   same, channels_last
   dw_cfg4        depthwise bf16 ConvNeXt-T stages at N=256, batch sharded
                  over the GPUs (weak in the sense of fixed total work: strong)
-  iterate_cfg5   one Jacobi step of the 32768^2 fp32 grid, row bands over the
-                 GPUs with a 3-row halo exchange (strong scaling)
   dw_k3          3x3 depthwise fp32 1x32x1024x1024, no bias: the operator and
                  input recipe of the reference's MetaSchedule benchmark
                  (benchmark/MetaSchedule/depthwise_conv.py, common.py)
@@ -26,10 +30,11 @@ one JSON line.  Workloads (the benchmark configurations; synthetic seeded inputs
 
 A "step" is one pass of the hot path over one batch of input already resident
 in HBM; consecutive steps rotate over enough buffer sets that every step's
-inputs are out of L2 (footprint > 2 x 126 MB).  The K timed steps are captured
-as one CUDA graph and replayed once (stream launches with --no-graph; always
-for the multi-GPU iterated stencil); the line also gives the stream-launch
-time of the same K steps (`stream_ms_per_step`).  `value` is whole-job
+inputs are out of L2 (footprint > 2 x 126 MB; the iterated stencil's 4 GiB
+grid is far larger).  The K timed steps of the single-launch workloads are
+captured as one CUDA graph and replayed once (stream launches with --no-graph;
+always for the iterated stencil); the line also gives the stream-launch time
+of the same K steps (`stream_ms_per_step`).  `value` is whole-job
 compulsory bytes (input + output + weights + bias) / device time (CUDA events,
 max over ranks).  `e2e` repeats the measurement through the public API with
 pinned host buffers, host<->device copies inside the timed region.
@@ -57,7 +62,7 @@ METRIC = "achieved HBM GB/s (% of roofline) and GPoints/s at 1/2/4/8 B200 vs CPU
 L2_BYTES = 126 * 1024 * 1024
 NOMINAL_HBM_GBS = 8000.0
 FALLBACK_HBM_GBS = 6650.0
-FMA_PER_SM_PER_CLK = 128  # measured on this pool: 124-127 FFMA/clk/SM
+FMA_PER_SM_PER_CLK = 128  # B200 FP32 lanes per SM (a microbenchmark reads 124-127 FFMA/clk/SM)
 TAPS = 49
 
 
@@ -645,44 +650,55 @@ class DwLnCfg4(DwCfg4):
 
 
 class IterateCfg5:
-    """one Jacobi step of the 32768^2 fp32 grid, row-band partitioned."""
+    """the 32768^2 fp32 iterated stencil (seed 4), row-band partitioned.
+
+    A step is one Jacobi step of the whole grid: every rank advances its band
+    (BandedStencil; at N > 1 one fused kernel per step that also stores the
+    band's edge rows into the neighbours' halos over NVLink).  The e2e job is
+    the configuration's whole job through the same public API: the band from
+    pinned host memory, 100 steps, the band back to pinned host memory.
+    """
 
     name = "iterate7x7_cfg5_32768x32768_f32_step"
     dtype = "f32"
     scaling = "strong"
+    job_steps = 100    # the configuration's time steps
+    parity_steps = 2
 
     def __init__(self, rank, world, dev, H=32768):
-        from pla_b200.iterate import BandedStencil
+        from pla_b200.iterate import band_rows
 
         self.H = self.W = H
+        self.name = f"iterate7x7_cfg5_{H}x{H}_f32_step"
+        self.rank, self.world, self.dev = rank, world, dev
         g = torch.Generator().manual_seed(4)
-        # Only this rank's band (+ halo) is materialised on the host.
-        bs_probe = __import__("pla_b200.iterate", fromlist=["band_rows"]).band_rows(H, world, rank)
-        a0, a1 = max(0, bs_probe[0] - 3), min(H, bs_probe[1] + 3)
-        x = self._rows(g, a0, a1)
+        self.r0, self.r1 = band_rows(H, world, rank)
+        self.rows = self.r1 - self.r0
+        # Grid rows [s0, s1) on the host: the band, its 3 halo rows and 3 more
+        # on each side (a two-step parity check of an edge row reads 6 rows
+        # past it).  Pinned: the e2e job copies the band from here.
+        self.s0, self.s1 = max(0, self.r0 - 6), min(H, self.r1 + 6)
+        self.slab = self._rows(g, self.s0, self.s1, pin=dev is not None)
         w = torch.rand(7, 7, generator=g) * 2 - 1
-        w = w / w.sum()
-        self.w_cpu = w
-        r0, r1 = bs_probe
-        self.rows = r1 - r0
-        band = torch.zeros(self.rows + 6, self.W)
-        off = 3 - (r0 - a0)
-        band[off:off + (a1 - a0)].copy_(x)
-        self.band_cpu = band
+        self.w_cpu = w / w.sum()
         self.points = self.rows * self.W
         self.bytes = compulsory_bytes(self.points, self.points, 4, TAPS, 0, 4)
         self.nsets = 1
-        self.launches_per_step = 3 if world > 1 else 1
+        self.launches_per_step = 1
         if dev is None:  # CPU reference arm only
             return
-        self.bs = BandedStencil(H, self.W, w.to(dev), group=None, device=dev)
-        self.bs.bufs[self.bs.cur].copy_(band)
+        from pla_b200.iterate import BandedStencil
 
-    def _rows(self, g, a0, a1):
+        self.bs = BandedStencil(H, self.W, self.w_cpu.to(dev), group=None, device=dev)
+        if world > 1 and self.bs.mode != "p2p":
+            self.launches_per_step = 3  # edge rows, interior, edge rows (NCCL exchange on a side stream)
+        self.bs.load(self.slab, row0=self.s0)
+
+    def _rows(self, g, a0, a1, pin=False):
         # Rows a0..a1 of the seeded U(-1,1) grid, drawn in grid order (row blocks).
         # Every rank draws the same full sequence but keeps only its rows, in
         # chunks, so no rank holds the 4 GiB grid.
-        out = torch.empty(a1 - a0, self.W)
+        out = torch.empty(a1 - a0, self.W, pin_memory=pin)
         chunk = 1024
         for r in range(0, self.H, chunk):
             blk = torch.rand(min(chunk, self.H - r), self.W, generator=g) * 2 - 1
@@ -699,17 +715,70 @@ class IterateCfg5:
         self.bs.close()
 
     def config(self):
+        if self.world == 1:
+            par = "one band (the whole grid) on one GPU, zero halos (Dirichlet boundary)"
+        elif self.bs.mode == "p2p":
+            par = ("row bands, 3-row halo exchange per step fused into the step kernel (edge tiles first, "
+                   "rows stored into the neighbours' halos over NVLink via CUDA IPC, flag handshake; no "
+                   "collective call)")
+        else:
+            par = "row bands, 3-row halo exchange per step (NCCL send/recv on a side stream, overlapped with " \
+                  "interior rows)"
         return {"workload": self.name, "shape": [self.H, self.W], "seed": 4, "x": "U(-1,1)",
-                "w": "U(-1,1) normalised to sum 1", "bias": False,
-                "l2": "4 GiB grid per buffer >> 126 MB L2",
-                "parallelism": "row bands, 3-row halo exchange per step fused into the step kernel "
-                               "(edge tiles first, rows stored into the neighbours' halos over NVLink via "
-                               "CUDA IPC, flag handshake; no collective call)" if self.bs.mode == "p2p" else
-                               "row bands, 3-row halo exchange per step (NCCL send/recv on a side stream, "
-                               "overlapped with interior rows)"}
+                "w": "U(-1,1) normalised to sum 1", "bias": False, "steps_per_job": self.job_steps,
+                "l2": f"{self.H * self.W * 4 >> 20} MiB grid per buffer (> 126 MB L2 from 6144^2 up)",
+                "parallelism": par}
 
+    # -- end to end: the configuration's whole job through the public API --
     def e2e_setup(self):
-        raise NotImplementedError
+        a0, a1 = self.bs.halo_span()
+        self.host_out = torch.empty(self.rows, self.W, pin_memory=True)
+        self.h2d_job = (a1 - a0) * self.W * 4
+        self.d2h_job = self.host_out.numel() * 4
+
+    def e2e_job(self):
+        """Band + halo rows pinned host -> device, job_steps steps, band -> pinned host (current stream)."""
+        self.bs.load_async(self.slab, self.s0)
+        self.bs.run(self.job_steps)
+        self.host_out.copy_(self.bs.band(), non_blocking=True)
+
+    # -- parity: the CPU oracle is the checker here, after all timing -------
+    def parity_segments(self):
+        """Band rows checked: the 3 edge rows at each end, the 3 rows inside
+        each of them (the rows next to the halo exchange) and 4 seeded interior
+        rows, as [c0, c1) segments."""
+        R = self.rows
+        segs = [(0, min(6, R)), (max(0, R - 6), R)]
+        inner = list(range(6, R - 6))
+        pick = np.random.default_rng(4 + self.rank).choice(len(inner), size=min(4, len(inner)), replace=False) \
+            if inner else []
+        segs += [(inner[k], inner[k] + 1) for k in sorted(pick)]
+        return segs
+
+    def parity(self):
+        """Reload the seeded grid, run parity_steps steps and compare rows of
+        this rank's band bit for bit with the CPU oracle (oracle/pla_oracle.c)
+        run on the grid rows they depend on."""
+        from oracle import oracle
+
+        self.bs.load(self.slab, row0=self.s0)
+        self.bs.run(self.parity_steps)
+        if self.bs.device.type == "cuda":
+            torch.cuda.synchronize(self.bs.device)
+            self.bs.check_faults()
+        n, bad = 0, []
+        reach = 3 * self.parity_steps
+        for c0, c1 in self.parity_segments():
+            g0, g1 = self.r0 + c0, self.r0 + c1
+            i0, i1 = max(0, g0 - reach), min(self.H, g1 + reach)
+            sub = self.slab[i0 - self.s0:i1 - self.s0].contiguous()
+            ref = oracle.stencil7x7_iterate(sub, self.w_cpu, self.parity_steps)[g0 - i0:g1 - i0]
+            got = self.bs.band()[c0:c1].cpu()
+            n += c1 - c0
+            if not torch.equal(got, ref):
+                bad.append(f"rank {self.rank} grid rows [{g0}, {g1}): "
+                           f"{int((got != ref).sum())} of {got.numel()} points differ")
+        return {"rows_checked": n, "mismatches": bad}
 
     def cpu_reference(self):
         from oracle.reference_modules import StencilModel
@@ -718,13 +787,17 @@ class IterateCfg5:
         with torch.no_grad():
             m.conv1.weight.copy_(self.w_cpu.view(1, 1, 7, 7))
             m.conv1.bias = None
-        band = self.band_cpu
-        rows = self.rows
+        slab, rows, off = self.slab, self.rows, self.r0 - self.s0
 
         def run_rows(r0, r1):
+            # band rows [r0, r1) from grid rows r0 - 3 .. r1 + 3 (zero rows
+            # outside the grid, as the Dirichlet boundary)
+            a0, a1 = off + r0 - 3, off + r1 + 3
+            x = slab[max(0, a0):min(slab.shape[0], a1)]
+            if a0 < 0 or a1 > slab.shape[0]:
+                x = torch.nn.functional.pad(x, (0, 0, max(0, -a0), max(0, a1 - slab.shape[0])))
             with torch.no_grad():
-                out = m(band[r0:r1 + 6].view(1, 1, r1 - r0 + 6, self.W))
-            return out
+                return m(x.reshape(1, 1, r1 - r0 + 6, self.W))
 
         def bytes_rows(n):
             return compulsory_bytes(n * self.W, n * self.W, 4, TAPS, 0, 4)
@@ -793,8 +866,10 @@ def main():
     ap.add_argument("--steps", type=int, default=400)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="stencil_cfg2")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="iterate_cfg5")
     ap.add_argument("--e2e-steps", type=int, default=20)
+    ap.add_argument("--grid", type=int, default=32768,
+                    help="iterate_cfg5 grid side (32768 is the configuration; smaller for profiling captures)")
     ap.add_argument("--cpu-budget", type=float, default=15.0, help="seconds of CPU work for cpu_baseline")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="time the K steps as stream launches, no CUDA graph")
@@ -817,7 +892,7 @@ def main():
 
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
 
-    wl = Wl(rank, world, dev)
+    wl = Wl(rank, world, dev, H=args.grid) if Wl is IterateCfg5 else Wl(rank, world, dev)
     # Workloads whose step is one plain launch per stage run their K timed
     # steps as one CUDA graph (captured once, replayed once): the graph holds
     # exactly those K steps' launches with the same bound arguments, and the
@@ -907,7 +982,32 @@ def main():
 
     # ---- end to end through the public API, pinned host buffers ----------
     e2e = None
-    try:
+    if hasattr(wl, "e2e_job"):
+        # The configuration's whole job (H2D of the inputs, all its steps, D2H
+        # of the result) per timed region; the copies are amortised over the
+        # job's steps.
+        wl.e2e_setup()
+        barrier()
+        wl.e2e_job()  # untimed
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        wl.e2e_job()
+        e1.record(stream)
+        barrier()
+        e_ms = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(e_ms, op=dist.ReduceOp.MAX)
+        J = wl.job_steps
+        e_step = e_ms.item() / J
+        e2e = {"value": job_bytes / (e_step * 1e-3) / 1e9, "unit": "GB/s", "gpoints_per_s":
+               job_points / (e_step * 1e-3) / 1e9, "ms_per_step": e_step, "steps": J, "ms_per_job": e_ms.item(),
+               "h2d_bytes_per_step": int(wl.h2d_job // J), "d2h_bytes_per_step": int(wl.d2h_job // J),
+               "h2d_bytes_per_job": int(wl.h2d_job), "d2h_bytes_per_job": int(wl.d2h_job),
+               "path": f"per rank: band + halo rows pinned host -> device, {J} Jacobi steps through "
+                       f"BandedStencil.run, band -> pinned host, all in one timed region (max over ranks); "
+                       f"bytes per step = bytes per job / {J}"}
+    else:
         wl.e2e_setup()
         s_in, s_cmp, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev), torch.cuda.Stream(dev)
         evs = {"in_done": [None, None], "cmp_done": [None, None], "out_done": [None, None]}
@@ -933,8 +1033,25 @@ def main():
                "h2d_bytes_per_step": int(wl.h2d_bytes), "d2h_bytes_per_step": int(wl.d2h_bytes),
                "path": "pinned host -> H2D (stream A) -> public API call (stream B) -> D2H (stream C), "
                        "double-buffered"}
-    except NotImplementedError:
-        e2e = None
+
+    # ---- parity: after all timing, the CPU oracle checks rows of the result
+    parity = None
+    if hasattr(wl, "parity"):
+        res = wl.parity()
+        bad = torch.tensor([len(res["mismatches"])], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(bad, op=dist.ReduceOp.SUM)
+            lists = [None] * world
+            dist.all_gather_object(lists, res["mismatches"])
+            mism = [m for lst in lists for m in lst]
+        else:
+            mism = res["mismatches"]
+        parity = {"status": "ok" if bad.item() == 0 else "MISMATCH", "mismatches": mism[:8],
+                  "rows_checked_per_rank": res["rows_checked"],
+                  "what": f"after the timed region: the seeded grid reloaded, {wl.parity_steps} steps, then "
+                          "every rank's 3 edge rows at each end, the 3 rows inside them and 4 seeded interior "
+                          "rows compared bit for bit with the CPU oracle (oracle/pla_oracle.c) run on the grid "
+                          "rows they depend on"}
 
     clocks = clk.summary()
     peak, peak_kind = measured_peaks()
@@ -986,6 +1103,7 @@ def main():
                          "fma_ceiling_gpoints_per_s": fma_gpts,
                          "fma_frac": (job_points / world) / (mean_step_ms * 1e-3) / 1e9 / fma_gpts},
             "cpu_baseline": cpu_baseline, "e2e": e2e, **({"unfused_pair": unfused} if unfused else {}),
+            **({"parity": parity} if parity else {}),
             "gpu_launches": K * wl.launches_per_step, "clocks": clocks,
             "launch_mode": "one CUDA graph of the K steps, replayed once" if use_graph else "stream launches",
             **({"stream_ms_per_step": stream_ms_per_step} if stream_ms_per_step is not None else {}),
@@ -997,6 +1115,8 @@ def main():
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+    if parity and parity["status"] != "ok":
+        return 3
 
 
 def run_reference(args, Wl, rank, world):
@@ -1004,7 +1124,7 @@ def run_reference(args, Wl, rank, world):
     data/stencil_7x7.py / data/depthwise_conv_7x7.py) on the host cores."""
     if rank != 0:
         return 0
-    wl = Wl(0, 1, None)
+    wl = Wl(0, 1, None, H=args.grid) if Wl is IterateCfg5 else Wl(0, 1, None)
     budget = 120.0
     gbs, cpu = time_cpu_reference(wl, budget, steps=args.steps, warmup=args.warmup)
     s_per = cpu["s_per_call"]

@@ -88,8 +88,9 @@ PLA_API int pla_version(void);
  * (element strides sn, sh, sw; sn ignored when n == 1), y is contiguous
  * [n, h, width], w holds 49 taps row-major, b is NULL or one element, all of
  * dtype `dtype` (enum pla_dtype).  y must not overlap x (as with the
- * reference, whose extension allocates a fresh output).  Unlike the
- * reference it returns a status.
+ * reference, whose extension allocates a fresh output): overlapping byte
+ * spans return PLA_ERR_INVALID_ARGUMENT.  Unlike the reference it returns a
+ * status.
  */
 PLA_API int pla_stencil7x7_forward(const void* x, const void* w, const void* b, void* y,
                            int n, int h, int width,
@@ -122,7 +123,8 @@ PLA_API int pla_stencil7x7_forward_taps(const void* x, const float* taps, const 
  *    model_cutlass_autotune_v5.py:403-420).
  * Differences: w is the module's own [C,1,7,7] weight (no [C,8,80] repack),
  * b may be non-NULL ([C]), dtype may be f32/bf16/f16/f64 and layout NCHW or
- * NHWC.  x and y are dense in `layout` and must not overlap.
+ * NHWC.  x and y are dense in `layout` and must not overlap
+ * (PLA_ERR_INVALID_ARGUMENT otherwise).
  */
 PLA_API int pla_depthwise7x7_forward(const void* x, const void* w, const void* b, void* y,
                              int n, int c, int h, int width,
@@ -179,7 +181,8 @@ PLA_API int pla_depthwise7x7_layernorm_nhwc(const void* x, const void* w, const 
  *     u_0 = x;  u_{t+1} = stencil(u_t; w) (+ b if non-NULL);  y = u_steps
  * fp32/bf16/f16 planes [h, width], contiguous.  `scratch` is a caller-owned
  * device buffer of at least h*width elements used as the second ping-pong
- * buffer; x is only read; y may alias x.
+ * buffer; x is only read; y may be x itself.  A partial overlap of x and y,
+ * or a scratch overlapping either, returns PLA_ERR_INVALID_ARGUMENT.
  */
 PLA_API int pla_stencil7x7_iterate(const void* x, const void* w, const void* b, void* y,
                            void* scratch, int h, int width, int steps,
@@ -201,7 +204,8 @@ PLA_API int pla_stencil7x7_iterate(const void* x, const void* w, const void* b, 
  *
  * The first call on a device looks up the array's device address
  * (cudaGetSymbolAddress) with that device current; make that first call
- * before any stream capture.  All calls on a device share the one array and
+ * before any stream capture.  Only a successful lookup is kept: after a
+ * failed one the next call tries again.  All calls on a device share the one array and
  * leave the last call's data in it (no call needs it cleared: every step
  * overwrites the whole plane before reading it), so calls that overlap on
  * the GPU (concurrent streams) race on it; serialise them.
@@ -225,6 +229,7 @@ PLA_API int pla_stencil7x7_iterate_taps(const void* x, const float* taps, const 
  * rows rows+3..rows+5 the halo rows below it.  The step writes output band
  * rows [row_begin, row_end) (0 <= row_begin <= row_end <= rows) into
  * out rows 3+row_begin .. 3+row_end-1; halo rows of `out` are not touched.
+ * `in` and `out` must not overlap (PLA_ERR_INVALID_ARGUMENT).
  */
 PLA_API int pla_stencil7x7_band_step(const void* in, const void* w, const void* b, void* out,
                              int rows, int width, int row_begin, int row_end,

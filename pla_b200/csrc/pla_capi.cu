@@ -109,6 +109,27 @@ size_t dtype_size(int dtype) {
 
 bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
+// Byte span [lo, hi) touched by a tensor view; overlap tests between spans.
+struct Span {
+  uintptr_t lo, hi;
+};
+Span dense_span(const void* p, long long elems, size_t es) {
+  const uintptr_t b = reinterpret_cast<uintptr_t>(p);
+  return {b, b + static_cast<uintptr_t>(elems) * es};
+}
+// (extent, element stride) per dimension; strides may be negative.
+Span strided_span(const void* p, size_t es, int nd, const long long* ext, const long long* str) {
+  long long lo = 0, hi = 0;
+  for (int i = 0; i < nd; ++i) {
+    if (ext[i] <= 0) return {0, 0};
+    const long long d = (ext[i] - 1) * str[i] * static_cast<long long>(es);
+    if (d < 0) lo += d; else hi += d;
+  }
+  const uintptr_t b = reinterpret_cast<uintptr_t>(p);
+  return {b + static_cast<uintptr_t>(lo), b + static_cast<uintptr_t>(hi) + es};
+}
+bool overlap(Span a, Span b) { return a.lo < b.hi && b.lo < a.hi; }
+
 // Per-(kernel, device) one-time attribute setup (dynamic smem opt-in) and
 // the resident-CTA count used to size persistent grids.
 template <auto Kernel>
@@ -833,6 +854,13 @@ int stencil_forward_impl(const void* x, const void* w, const void* b, const Host
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const long long plane = static_cast<long long>(h) * width;
   if (n == 1) sn = plane;  // ignored for a single plane
+  {
+    // The output must not overlap the input: a tile's halo rows are read
+    // after other CTAs may already have stored their outputs.
+    const long long ext[3] = {n, h, width}, str[3] = {sn, sh, sw};
+    if (overlap(strided_span(x, dtype_size(dtype), 3, ext, str), dense_span(y, n * plane, dtype_size(dtype))))
+      return PLA_ERR_INVALID_ARGUMENT;
+  }
   if (sw == 1 && tile_path_ok(x, y, dtype, width, sh, sn, n)) {
     return launch_tile_dtype(dtype, x, w, b, ht, y, n, 1, h, width, sh, sn, 0, h, 0, plane, width, s);
   }
@@ -856,6 +884,7 @@ int band_step_impl(const void* in, const void* w, const void* b, const HostTaps*
   if (!in || (!w && !ht) || !out) return PLA_ERR_INVALID_ARGUMENT;
   const size_t es = dtype_size(dtype);
   const long long band = static_cast<long long>(rows + 6) * width;
+  if (overlap(dense_span(in, band, es), dense_span(out, band, es))) return PLA_ERR_INVALID_ARGUMENT;
   void* out_rows = static_cast<char*>(out) + 3ll * width * es;
   if (!tile_path_ok(in, out_rows, dtype, width, width, band, 1)) return PLA_ERR_UNSUPPORTED;
   return launch_tile_dtype(dtype, in, w, b, ht, out_rows, 1, 1, rows + 6, width, width, band, row_begin, row_end,
@@ -871,6 +900,15 @@ int iterate_impl(const void* x, const void* w, const void* b, const HostTaps* ht
   if (!x || (!w && !ht) || !y || (!scratch && steps > 0)) return PLA_ERR_INVALID_ARGUMENT;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const size_t bytes = static_cast<size_t>(plane) * dtype_size(dtype);
+  {
+    // y may be x itself, but not overlap it partially; scratch overlaps neither.
+    const Span sx = dense_span(x, plane, dtype_size(dtype)), sy = dense_span(y, plane, dtype_size(dtype));
+    if (x != y && overlap(sx, sy)) return PLA_ERR_INVALID_ARGUMENT;
+    if (steps > 0) {
+      const Span ss = dense_span(scratch, plane, dtype_size(dtype));
+      if (overlap(ss, sx) || overlap(ss, sy)) return PLA_ERR_INVALID_ARGUMENT;
+    }
+  }
   if (steps == 0) {
     if (x != y) PLA_CUDA(cudaMemcpyAsync(y, x, bytes, cudaMemcpyDeviceToDevice, s));
     return PLA_OK;
@@ -900,23 +938,28 @@ static_assert(kNoAllocScratchBytes == PLA_NOALLOC_SCRATCH_BYTES, "header and lib
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
 struct NoAllocScratch {
-  std::once_flag once;
-  cudaError_t err = cudaSuccess;
-  void* ptr = nullptr;
+  std::mutex mu;
+  void* ptr = nullptr;  // set once, by the first successful lookup
 };
 NoAllocScratch g_noalloc[kMaxDevices];
 
 // Device address of g_noalloc_scratch on the current device.  The host-side
 // name of the array is only a stand-in for the symbol, so the address must
-// come from cudaGetSymbolAddress, looked up once per device with that device
-// current (on the first call made on that device).
+// come from cudaGetSymbolAddress, looked up with that device current (on the
+// first call made on that device).  Only a successful lookup is kept: a
+// failed one (e.g. made during a stream capture) is retried by the next call.
 int noalloc_scratch(void** out) {
   int dev;
   int st = current_device(&dev);
   if (st != PLA_OK) return st;
   NoAllocScratch& s = g_noalloc[dev];
-  std::call_once(s.once, [&]() { s.err = cudaGetSymbolAddress(&s.ptr, g_noalloc_scratch); });
-  if (s.err != cudaSuccess) return cuda_fail(s.err, "cudaGetSymbolAddress(g_noalloc_scratch)");
+  std::lock_guard<std::mutex> lock(s.mu);
+  if (!s.ptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(g_noalloc_scratch)");
+    s.ptr = p;
+  }
   *out = s.ptr;
   return PLA_OK;
 }
@@ -969,6 +1012,8 @@ int pla_depthwise7x7_forward(const void* x, const void* w, const void* b, void* 
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const long long plane = static_cast<long long>(h) * width;
   const long long planes = static_cast<long long>(n) * c;
+  if (overlap(dense_span(x, planes * plane, dtype_size(dtype)), dense_span(y, planes * plane, dtype_size(dtype))))
+    return PLA_ERR_INVALID_ARGUMENT;
   if (dtype != PLA_F64) {
     if (stack_path_ok(x, y, dtype, layout, n, c, h, width))
       return launch_stack_dtype(dtype, layout == PLA_NHWC, x, w, b, y, n, c, h, s);
@@ -1019,6 +1064,8 @@ int pla_depthwise_forward(const void* x, const void* w, const void* b, void* y, 
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const long long plane = static_cast<long long>(h) * width;
   const long long planes = static_cast<long long>(n) * c;
+  if (overlap(dense_span(x, planes * plane, dtype_size(dtype)), dense_span(y, planes * plane, dtype_size(dtype))))
+    return PLA_ERR_INVALID_ARGUMENT;
   // Dense NCHW planes wide enough for the tile shapes: the TMA tile kernel
   // with a k x k filter.  Everything else (NHWC, small or misaligned planes,
   // fp64): the one-thread-per-output kernel.
@@ -1051,6 +1098,11 @@ int pla_depthwise7x7_layernorm_nhwc(const void* x, const void* w, const void* b,
   if (static_cast<long long>(n) * c * h * width == 0) return PLA_OK;
   if (!x || !w || !y) return PLA_ERR_INVALID_ARGUMENT;
   if (h > (1 << 30) || width > (1 << 30)) return PLA_ERR_TOO_LARGE;
+  {
+    const long long elems = static_cast<long long>(n) * c * h * width;
+    if (overlap(dense_span(x, elems, dtype_size(dtype)), dense_span(y, elems, dtype_size(dtype))))
+      return PLA_ERR_INVALID_ARGUMENT;
+  }
   LnArgs ln;
   ln.gamma = gamma;
   ln.beta = beta;
@@ -1101,6 +1153,10 @@ int pla_stencil7x7_iterate_noalloc(const void* x, const void* w, const void* b, 
     return PLA_ERR_TOO_LARGE;
   }
   if (bytes == 0) return PLA_OK;
+  if (!x || !w || !y) return PLA_ERR_INVALID_ARGUMENT;
+  if (x != y && overlap(dense_span(x, bytes / dtype_size(dtype), dtype_size(dtype)),
+                        dense_span(y, bytes / dtype_size(dtype), dtype_size(dtype))))
+    return PLA_ERR_INVALID_ARGUMENT;
   void* scratch = nullptr;
   const int st = noalloc_scratch(&scratch);
   if (st != PLA_OK) return st;
@@ -1116,6 +1172,7 @@ int pla_stencil7x7_band_step_halo(const void* in, const float* taps, const float
   if ((up_out && (!up_flags || up_rows < 3)) || (down_out && !down_flags)) return PLA_ERR_INVALID_ARGUMENT;
   const size_t es = dtype_size(dtype);
   const long long band = static_cast<long long>(rows + 6) * width;
+  if (overlap(dense_span(in, band, es), dense_span(out, band, es))) return PLA_ERR_INVALID_ARGUMENT;
   void* out_rows = static_cast<char*>(out) + 3ll * width * es;
   if (!tile_path_ok(in, out_rows, dtype, width, width, band, 1)) return PLA_ERR_UNSUPPORTED;
   if ((up_out && !aligned(up_out, 16)) || (down_out && !aligned(down_out, 16))) return PLA_ERR_UNSUPPORTED;

@@ -203,15 +203,52 @@ class BandedStencil:
         return peer if self.group is None else dist.get_global_rank(self.group, peer)
 
     # -- state -------------------------------------------------------------
-    def load(self, grid: torch.Tensor) -> None:
-        """Copy this rank's band (and its halo rows) out of the full grid [H, W]."""
+    def halo_span(self) -> tuple[int, int]:
+        """Grid rows [a0, a1) this rank loads: its band and the halo rows that exist."""
+        return max(0, self.r0 - 3), min(self.H, self.r1 + 3)
+
+    def load(self, grid: torch.Tensor, row0: int = 0) -> None:
+        """Copy this rank's band and its halo rows out of `grid`.
+
+        ``grid`` holds grid rows [row0, row0 + grid.shape[0]) of the [H, W]
+        grid: the whole grid (row0 = 0) or any slab covering ``halo_span()``
+        (host or device memory).
+
+        In p2p mode a neighbour's last step may still be storing its edge rows
+        into this rank's halo rows over peer memory; once any step has run,
+        every rank first drains its stream and meets the others at a barrier,
+        so no late store lands on the freshly loaded rows.  Collective then:
+        every rank calls it.
+        """
+        a0, a1 = self.halo_span()
+        if grid.dim() != 2 or grid.shape[1] != self.W or row0 > a0 or row0 + grid.shape[0] < a1:
+            raise ValueError(f"grid rows [{row0}, {row0 + grid.shape[0]}) do not cover rows [{a0}, {a1})")
+        if self.mode == "p2p" and (self._armed or self.step_idx > 0):
+            torch.cuda.synchronize(self.device)
+            dist.barrier(group=self.group)
         b = self.bufs[self.cur]
         b.zero_()
-        a0, a1 = max(0, self.r0 - 3), min(self.H, self.r1 + 3)
-        b[3 - (self.r0 - a0):3 + self.rows + (a1 - self.r1)].copy_(grid[a0:a1])
+        b[3 - (self.r0 - a0):3 + self.rows + (a1 - self.r1)].copy_(grid[a0 - row0:a1 - row0])
         self.bufs[1 - self.cur].zero_()
         if self.mode == "p2p":
             self._armed = False  # neighbours must finish loading before anyone steps
+
+    def load_async(self, host_rows: torch.Tensor, row0: int, stream: torch.cuda.Stream | None = None) -> None:
+        """Stream-ordered copy of this rank's band and halo rows from pinned host
+        memory into the current buffer, with no barrier and no zeroing.
+
+        For a repeated job on an already loaded band (the halo rows outside
+        the grid stay zero from ``load``): the caller has synchronised every
+        rank since the last step, and the steps that follow on the same
+        stream see the copy.  ``host_rows`` holds grid rows
+        [row0, row0 + host_rows.shape[0]).
+        """
+        a0, a1 = self.halo_span()
+        if row0 > a0 or row0 + host_rows.shape[0] < a1:
+            raise ValueError("host rows do not cover this rank's band and halo")
+        dst = self.bufs[self.cur][3 - (self.r0 - a0):3 + self.rows + (a1 - self.r1)]
+        with torch.cuda.stream(stream or torch.cuda.current_stream(self.device)):
+            dst.copy_(host_rows[a0 - row0:a1 - row0], non_blocking=True)
 
     def band(self) -> torch.Tensor:
         """This rank's current band rows [rows, W] (a view)."""

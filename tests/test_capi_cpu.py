@@ -189,3 +189,79 @@ def test_bench_reference_arm_line_on_cpu():
     assert d["value"] > 0 and d["cpu_baseline"]["value"] == d["value"]
     assert d["e2e"] == {"value": d["value"], "unit": d["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
     assert d["config"]["workload"] == "depthwise7x7_cfg1_1x96x56x56_f32"
+
+
+def _bench_module():
+    import importlib.util
+
+    spec = importlib.util.spec_from_file_location("bench_mod", os.path.join(ROOT, "bench.py"))
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    return bench
+
+
+def test_bench_iterate_parity_leg_on_cpu_bands():
+    """The iterated-stencil bench line's parity leg: segments cover the band
+    edges and the rows inside them, the slab reaches 6 rows past the band, and
+    the check passes on a correct band and names the rows of a planted
+    mistake (planted in the oracle's own band step, on the CPU)."""
+    from oracle import oracle
+    from pla_b200.iterate import BandedStencil
+
+    bench = _bench_module()
+    H = 96
+    for world, rank in ((1, 0), (3, 1), (3, 2)):
+        wl = bench.IterateCfg5(rank, world, None, H=H)
+        assert (wl.s0, wl.s1) == (max(0, wl.r0 - 6), min(H, wl.r1 + 6))
+        segs = wl.parity_segments()
+        rows = sorted(r for a, b in segs for r in range(a, b))
+        assert rows[:6] == list(range(6)) and rows[-6:] == list(range(wl.rows - 6, wl.rows))
+        assert len(rows) == 12 + 4
+    # A single CPU band driven by the oracle's band step, as the kernel would.
+    wl = bench.IterateCfg5(0, 1, None, H=H)
+
+    def band_step(src, dst, rb, re):
+        dst[rb + 3:re + 3] = oracle.stencil7x7_rows(src, wl.w_cpu, rb + 3, re + 3)
+
+    wl.bs = BandedStencil(H, H, wl.w_cpu, device=torch.device("cpu"), step_fn=band_step)
+    res = wl.parity()
+    assert res["mismatches"] == [] and res["rows_checked"] == 16
+
+    def planted(src, dst, rb, re):
+        band_step(src, dst, rb, re)
+        dst[3 + 1, 5] += 1.0  # band row 1 is wrong after every step
+
+    wl.bs = BandedStencil(H, H, wl.w_cpu, device=torch.device("cpu"), step_fn=planted)
+    res = wl.parity()
+    assert len(res["mismatches"]) == 1 and "grid rows [0, 6)" in res["mismatches"][0]
+
+
+def test_overlapping_buffers_are_rejected_before_any_device_work():
+    """Every single-step entry rejects an output that overlaps its input, and
+    the iterate entries a partial x / y overlap or a scratch overlapping
+    either (the byte spans are compared before anything touches a device)."""
+    from pla_b200 import _lib
+
+    L = _lib.lib()
+    F32 = _lib.PLA_F32
+    base = 1 << 20  # never dereferenced: the checks return first
+    w = base + (1 << 19)
+    # 1 x 8 x 8 fp32 stencil: y starts 64 bytes into x
+    assert L.pla_stencil7x7_forward(base, w, None, base + 64, 1, 8, 8, 64, 8, 1, F32, None) == 1
+    # strided x (row stride 16) reaching into y
+    assert L.pla_stencil7x7_forward(base, w, None, base + 8 * 16 * 4 - 64, 1, 8, 8, 128, 16, 1, F32, None) == 1
+    taps = (ctypes.c_float * 49)()
+    assert L.pla_stencil7x7_forward_taps(base, taps, None, base, 1, 8, 8, 64, 8, 1, F32, None) == 1
+    assert L.pla_depthwise7x7_forward(base, w, None, base + 4, 2, 4, 8, 8, F32, _lib.PLA_NCHW, None) == 1
+    assert L.pla_depthwise_forward(base, w, None, base, 2, 4, 8, 8, 3, F32, _lib.PLA_NHWC, None) == 1
+    assert L.pla_depthwise7x7_layernorm_nhwc(base, w, None, None, None, 1e-6, base + 128, 1, 32, 7, 7, F32,
+                                             None) == 1
+    # iterate: partial x / y overlap, scratch overlapping x or y
+    assert L.pla_stencil7x7_iterate(base, w, None, base + 16, base + (1 << 16), 8, 8, 2, F32, None) == 1
+    assert L.pla_stencil7x7_iterate(base, w, None, base, base + 32, 8, 8, 2, F32, None) == 1
+    assert L.pla_stencil7x7_iterate_noalloc(base, w, None, base + 16, 8, 8, 2, F32, None) == 1
+    # band steps: in / out band buffers of (rows + 6) x width
+    assert L.pla_stencil7x7_band_step(base, w, None, base + 256, 64, 32, 0, 64, F32, None) == 1
+    flags = (ctypes.c_uint * 2)()
+    assert L.pla_stencil7x7_band_step_halo(base, taps, None, base + 256, 64, 32, F32, None, 0, None, flags, None,
+                                           None, flags, 0, None) == 1

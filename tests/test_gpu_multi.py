@@ -25,6 +25,11 @@ def _inputs(H, W):
     return x, w / w.sum()
 
 
+def _second_grid(H, W):
+    g = torch.Generator().manual_seed(5)
+    return torch.rand(H, W, generator=g) * 2 - 1
+
+
 def _rank(rank, world, port, H, W, steps, mode, q):
     import datetime
 
@@ -44,32 +49,44 @@ def _rank(rank, world, port, H, W, steps, mode, q):
         bs.load(x.to(dev))
         bs.run(steps)
         full = bs.gather()
+        # Reload a second grid right after the steps (p2p: the neighbours'
+        # last halo stores must not land on the new rows), from a host slab
+        # that holds only this rank's band and halo rows, and run again.
+        x2 = _second_grid(H, W)
+        a0, a1 = bs.halo_span()
+        bs.load(x2[a0:a1].clone(), row0=a0)
+        bs.run(steps + 1)
+        full2 = bs.gather()
         torch.cuda.synchronize()
         bs.check_faults()
         if rank == 0:
-            q.put(full.cpu())
+            q.put((full.cpu(), full2.cpu()))
         bs.close()
         dist.barrier()
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 @pytest.mark.parametrize("mode", ["p2p", "nccl"])
-@pytest.mark.parametrize("world,H,W,steps", [(2, 1000, 768, 9), (2, 300, 256, 12)])
+@pytest.mark.parametrize("world,H,W,steps", [(2, 1000, 768, 9), (2, 300, 256, 12), (4, 1000, 768, 9),
+                                             (8, 2048, 512, 7)])
 def test_banded_multi_gpu_equals_single_gpu(world, H, W, steps, mode):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     from pla_b200 import stencil7x7_iterate
 
     x, w = _inputs(H, W)
     ref = stencil7x7_iterate(x.cuda(), w.cuda(), steps).cpu()
+    ref2 = stencil7x7_iterate(_second_grid(H, W).cuda(), w.cuda(), steps + 1).cpu()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
     procs = [ctx.Process(target=_rank, args=(r, world, port, H, W, steps, mode, q)) for r in range(world)]
     for p in procs:
         p.start()
-    got = q.get(timeout=180)
+    got, got2 = q.get(timeout=180)
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
     assert torch.equal(got, ref)
+    assert torch.equal(got2, ref2)

@@ -80,8 +80,16 @@ def _rank_main(rank, world, port, H, W, steps, out_q):
         bs.load(x)
         bs.run(steps)
         full = bs.gather()
+        # Reload a second grid from a slab that holds only this rank's band
+        # and halo rows (as the benchmark does), and run again.
+        x2 = torch.rand(H, W, generator=g) * 2 - 1
+        a0, a1 = bs.halo_span()
+        lo, hi = max(0, a0 - 1), min(H, a1 + 2)
+        bs.load(x2[lo:hi].clone(), row0=lo)
+        bs.run(steps + 1)
+        full2 = bs.gather()
         if rank == 0:
-            out_q.put(full)
+            out_q.put((full, full2))
     finally:
         dist.destroy_process_group()
 
@@ -94,7 +102,7 @@ def test_banded_iterate_gloo_matches_single_domain(world, H, W, steps):
     procs = [ctx.Process(target=_rank_main, args=(r, world, port, H, W, steps, q)) for r in range(world)]
     for p in procs:
         p.start()
-    full = q.get(timeout=120)
+    full, full2 = q.get(timeout=120)
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
@@ -102,8 +110,20 @@ def test_banded_iterate_gloo_matches_single_domain(world, H, W, steps):
     x = torch.rand(H, W, generator=g) * 2 - 1
     w = torch.rand(7, 7, generator=g) * 2 - 1
     w = w / w.sum()
-    ref = oracle.stencil7x7_iterate(x, w, steps)
-    assert torch.equal(full, ref)
+    x2 = torch.rand(H, W, generator=g) * 2 - 1
+    assert torch.equal(full, oracle.stencil7x7_iterate(x, w, steps))
+    assert torch.equal(full2, oracle.stencil7x7_iterate(x2, w, steps + 1))
+
+
+def test_band_load_rejects_a_slab_that_misses_the_halo():
+    from pla_b200.iterate import BandedStencil
+
+    w = torch.rand(7, 7)
+    bs = BandedStencil(24, 16, w, device=torch.device("cpu"), step_fn=_oracle_band_step(w))
+    x = torch.rand(24, 16)
+    with pytest.raises(ValueError):
+        bs.load(x[2:], row0=2)  # one rank: its span is the whole grid, rows 0..1 missing
+    bs.load(x[:24], row0=0)
 
 
 # ---- a rank that leaves: the others get an error, not a hang -------------------
