@@ -9,8 +9,19 @@ replace ``data/depthwise_conv_7x7.py`` and ``data/stencil_7x7.py``.
 * ``pla_b200.iterate``   — ``stencil7x7_iterate()``, ``BandedStencil`` (multi-GPU)
 
 All compute goes through the C ABI in ``include/pla_b200.h``
-(``libpla_b200.so``, built by ``python -m pla_b200.build``).
+(``libpla_b200.so``, built by ``python -m pla_b200.build``).  The functional
+forms without ``out=`` run as torch custom ops, ``torch.ops.pla_b200.*``
+(``libpla_b200_torch.so``: TORCH_CHECK errors, device guard, current stream,
+Meta kernels for fake tensors), so they trace under ``torch.compile`` and
+replay in CUDA graphs with the weights current at replay time.
 """
+from . import _lib
+
+try:  # registered at import so that compiled code never traces the loading
+    _lib.ops()
+except ImportError:  # not built yet (e.g. while pla_b200.build runs): the ops raise when called
+    pass
+
 from .depthwise import DepthwiseLayerNorm, depthwise7x7, depthwise7x7_layernorm, depthwise_kxk
 from .iterate import BandedStencil, band_rows, stencil7x7_iterate
 from .stencil import stencil7x7

@@ -13,6 +13,7 @@ import torch
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libpla_b200.so")
+TORCH_LIB_PATH = os.path.join(_HERE, "libpla_b200_torch.so")
 
 PLA_F16, PLA_F32, PLA_F64, PLA_BF16 = 0, 1, 2, 3
 PLA_OK, PLA_ERR_UNSUPPORTED = 0, 2
@@ -74,6 +75,22 @@ def lib() -> ctypes.CDLL:
             fn.restype = restype
         _lib = handle
     return _lib
+
+
+_ops = None
+
+
+def ops():
+    """``torch.ops.pla_b200``: the torch custom ops of libpla_b200_torch.so
+    (csrc/torch_ops.cpp) over the C ABI, loaded once; raise if not built."""
+    global _ops
+    if _ops is None:
+        lib()
+        if not os.path.exists(TORCH_LIB_PATH):
+            raise ImportError(f"{TORCH_LIB_PATH} is missing: build it first (python -m pla_b200.build)")
+        torch.ops.load_library(TORCH_LIB_PATH)
+        _ops = torch.ops.pla_b200
+    return _ops
 
 
 def check(status: int, what: str) -> None:

@@ -48,6 +48,9 @@ def depthwise_kxk(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | No
 
     ``k`` defaults to ``weight.shape[-1]``; ``weight`` is [C,1,k,k] (or any
     shape with C*k*k elements).  Same layouts and dtypes as depthwise7x7.
+    Without ``out`` this is the torch op ``torch.ops.pla_b200.depthwise7x7``
+    (k = 7) or ``torch.ops.pla_b200.depthwise``; ``out`` writes into a caller
+    tensor through the same C ABI.
     """
     if not isinstance(x, torch.Tensor) or not x.is_cuda:
         raise ValueError("depthwise7x7 requires a CUDA input")
@@ -77,7 +80,9 @@ def depthwise_kxk(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | No
         x = x.contiguous()
         layout, fmt = _lib.PLA_NCHW, torch.contiguous_format
     if out is None:
-        out = torch.empty(x.shape, dtype=x.dtype, device=x.device, memory_format=fmt)
+        # torch op (device-resident filter, output in x's memory format)
+        op = _lib.ops().depthwise7x7 if k == 7 else _lib.ops().depthwise
+        return op(x, weight.detach().reshape(C, 1, k, k), None if bias is None else bias.detach())
     elif out.shape != x.shape or not out.is_contiguous(memory_format=fmt) or out.dtype != x.dtype:
         raise RuntimeError("out must match x's shape, dtype and memory format")
     elif _lib.overlaps(out, x):
@@ -123,7 +128,8 @@ def depthwise7x7_layernorm(x: torch.Tensor, weight: torch.Tensor, bias: torch.Te
         if t is not None and (not t.is_cuda or t.device != x.device or t.dtype != x.dtype or t.numel() != C):
             raise RuntimeError(f"{name} device/dtype/shape mismatch")
     if out is None:
-        out = torch.empty(x.shape, dtype=x.dtype, device=x.device, memory_format=torch.channels_last)
+        vecs = [None if t is None else t.detach() for t in (bias, norm_weight, norm_bias)]
+        return _lib.ops().depthwise7x7_layernorm(x, weight.detach(), *vecs, eps=float(eps))
     elif out.shape != x.shape or not out.is_contiguous(memory_format=torch.channels_last) or out.dtype != x.dtype:
         raise RuntimeError("out must match x's shape, dtype and channels_last format")
     elif _lib.overlaps(out, x):

@@ -43,8 +43,12 @@ def stencil7x7_iterate(x: torch.Tensor, weight: torch.Tensor, steps: int, bias: 
                        host_taps: _lib.HostTaps | None = None) -> torch.Tensor:
     """Apply the 7x7 stencil `steps` times to the CUDA grid x [H, W] (fp32/bf16/fp16).
 
-    The filter is copied to the host once per call (or taken from
-    ``host_taps``) so every step runs the constant-operand kernel.
+    Without ``out``, ``scratch`` and ``host_taps`` this is the torch op
+    ``torch.ops.pla_b200.stencil7x7_iterate`` (filter read from device
+    memory by every step; the op allocates the output and the second
+    ping-pong plane).  Otherwise the steps run the constant-operand kernel:
+    the filter is copied to the host once per call (a stream sync), or taken
+    from ``host_taps``.
     """
     if not isinstance(x, torch.Tensor) or not x.is_cuda:
         raise ValueError("stencil7x7_iterate requires a CUDA input")
@@ -57,6 +61,9 @@ def stencil7x7_iterate(x: torch.Tensor, weight: torch.Tensor, steps: int, bias: 
     if bias is not None and (bias.numel() != 1 or bias.dtype != x.dtype or bias.device != x.device):
         raise RuntimeError("bias device/dtype/shape mismatch")
     H, W = x.shape
+    if out is None and scratch is None and host_taps is None:
+        return _lib.ops().stencil7x7_iterate(x, weight.detach(), int(steps),
+                                             None if bias is None else bias.detach())
     if out is None:
         out = torch.empty_like(x)
     if scratch is None:
