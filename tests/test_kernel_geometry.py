@@ -122,9 +122,12 @@ def test_stack_kernel_rows_lanes_and_stage_copies():
             r, rg, g, lanes = _stack_geom(s, mix)
             rows = [grp * r + i for grp in range(rg) for i in range(r) if grp * r + i < s]
             assert sorted(rows) == list(range(s))
+            # The kernel's own mapping: warp = tid >> 5, lane group = warp / RG,
+            # row group = warp % RG, plane lane = group * 32 + lane; every
+            # (row group, plane lane) pair must belong to exactly one thread.
             warps = rg * g
-            lane_ids = sorted({(w // rg) * 32 + l for w in range(warps) for l in range(32)})
-            assert lane_ids == list(range(lanes))
+            pairs = [((tid >> 5) % rg, ((tid >> 5) // rg) * 32 + (tid & 31)) for tid in range(32 * warps)]
+            assert sorted(pairs) == [(a, b) for a in range(rg) for b in range(lanes)]
             plane = s * s
             stage_elems = lanes * plane
             assert (stage_elems * elem) % 16 == 0
@@ -170,3 +173,43 @@ def test_tile_kernel_covers_planes_and_reads_inside_the_box():
                                 assert (ty * th - k // 2 + box_row, tx * tw - left + box_col) == \
                                     (oy + ky - k // 2, ox + kx - k // 2)
                     assert len(seen) == h * w
+
+
+def test_restated_constants_match_the_kernel_sources():
+    """The constants and formulas restated above are read back from the
+    kernel sources, so a geometry change there fails here instead of leaving
+    these checks on stale numbers."""
+    import os
+    import re
+
+    csrc = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "pla_b200", "csrc")
+
+    def defs(name, struct=None):
+        text = open(os.path.join(csrc, name)).read()
+        if struct:  # only the definitions inside `struct <name> { ... };`
+            text = text[text.index(f"struct {struct} {{"):]
+            text = text[:text.index("};")]
+        out = {}
+        for m in re.finditer(r"constexpr\s+(?:int|bool|uint32_t)\s+(\w+)\s*=\s*([^;]+);", text):
+            out.setdefault(m.group(1), " ".join(m.group(2).split()))
+        return out
+
+    pair, stack, tile = defs("pair_kernel.cuh", "PairGeom"), defs("stack_kernel.cuh", "StackGeom"), \
+        defs("tile_kernel.cuh", "TileGeom")
+    tile["kTileThreads"] = defs("tile_kernel.cuh")["kTileThreads"]
+    capi_text = open(os.path.join(csrc, "pla_capi.cu")).read()
+    capi = dict(re.findall(r"\b(kWideR|kWideLX|kNarrowR|kNarrowLX|kShortR)\s*=\s*(\d+)", capi_text))
+    # PairGeom
+    assert (int(pair["S"]), int(pair["PL"]), int(pair["R"])) == (S, PL, R)
+    assert (pair["RG"], pair["CG"], pair["THREADS"]) == ("S / R", "S / 4", "PL * RG * CG")
+    assert (pair["LEFT"], pair["PITCH"], pair["ROWS"]) == ("16 / sizeof(T)", "S + 2 * LEFT", "S + 6")
+    # StackGeom (_stack_geom)
+    assert (stack["R"], stack["RG"], stack["G"]) == ("(S == 7) ? 7 : 2", "(S + R - 1) / R", "(S == 7) ? 4 : 1")
+    assert (stack["WARPS"], stack["LANES"]) == ("RG * G", "32 * G")
+    # TileGeom and the tile shapes the dispatcher instantiates
+    assert int(tile["kTileThreads"]) == 128
+    assert (tile["TW"], tile["TH"]) == ("4 * LX", "(kTileThreads / 32) * (32 / LX) * R")
+    assert (tile["ROWS"], tile["LEFT"], tile["PITCH"]) == ("TH + K - 1", "16 / sizeof(T)", "TW + 2 * LEFT")
+    shapes = {(int(capi["kWideR"]), int(capi["kWideLX"])), (int(capi["kNarrowR"]), int(capi["kNarrowLX"])),
+              (int(capi["kShortR"]), int(capi["kNarrowLX"]))}
+    assert shapes == {(8, 32), (7, 16), (2, 16)}
