@@ -117,11 +117,16 @@ def test_unsupported_inputs_raise():
 
     w = torch.randn(1024, 1, 7, 7, device=DEV)
     x = torch.randn(1, 1024, 14, 14, device=DEV).contiguous(memory_format=torch.channels_last)
-    with pytest.raises(_lib.PlaError):  # 32 channel groups: more CTAs than a cluster holds
+    # The functional form runs the torch op (TORCH_CHECK -> RuntimeError with
+    # the C ABI's status text); the out= form calls the C ABI through ctypes
+    # (PlaError, a RuntimeError).
+    with pytest.raises(RuntimeError, match="unsupported"):  # 32 channel groups: more CTAs than a cluster holds
         depthwise7x7_layernorm(x, w)
+    with pytest.raises(_lib.PlaError):
+        depthwise7x7_layernorm(x, w, out=torch.empty_like(x))
     with pytest.raises(RuntimeError):  # NCHW input
         depthwise7x7_layernorm(torch.randn(1, 32, 14, 14, device=DEV), torch.randn(32, 1, 7, 7, device=DEV))
-    with pytest.raises(_lib.PlaError):  # 12 bf16 channels: a 24-byte pixel row is not TMA-addressable
+    with pytest.raises(RuntimeError, match="unsupported"):  # 12 bf16 channels: 24-byte pixel rows, not TMA-addressable
         depthwise7x7_layernorm(torch.randn(1, 12, 14, 14, device=DEV).bfloat16()
                                .contiguous(memory_format=torch.channels_last),
                                torch.randn(12, 1, 7, 7, device=DEV).bfloat16())
