@@ -46,6 +46,16 @@ def _v2():
     return f
 
 
+def _record(**kv):
+    """Append one timing record (JSON line) to $PLA_HEAD_TO_HEAD_LOG when set."""
+    path = os.environ.get("PLA_HEAD_TO_HEAD_LOG")
+    if path:
+        import json
+
+        with open(path, "a") as f:
+            f.write(json.dumps(kv) + "\n")
+
+
 def _time(fn, iters=20, warmup=3):
     for _ in range(warmup):
         fn()
@@ -100,6 +110,10 @@ def test_against_reference_v7(H, W, dtype):
     print(f"\n[v7 {str(dtype)[6:]} {H}x{W}] reference launch_direct {t_ref * 1e3:.1f} us "
           f"({pts / t_ref / 1e6:.0f} GPt/s), pla_b200 {t_ours * 1e3:.1f} us ({pts / t_ours / 1e6:.0f} GPt/s), "
           f"speed-up {t_ref / t_ours:.2f}x")
+    _record(kernel="stencil", reference="v7 launch_direct", dtype=str(dtype)[6:], shape=[H, W],
+            reference_us=t_ref * 1e3, pla_b200_us=t_ours * 1e3, speedup=t_ref / t_ours)
+    # Same arithmetic, same box: this library's kernel must not be the slower one.
+    assert t_ours <= t_ref, f"pla_b200 {t_ours * 1e3:.1f} us slower than v7 {t_ref * 1e3:.1f} us"
 
 
 @pytest.mark.skipif(not os.path.exists(V2), reason="reference kernels not built (oracle/_ref)")
@@ -133,6 +147,9 @@ def test_against_reference_v2_fp16(H, W):
     print(f"\n[v2 fp16 {H}x{W}] reference launch_stencil (mma.sync) {t_ref * 1e3:.1f} us "
           f"({pts / t_ref / 1e6:.0f} GPt/s), pla_b200 {t_ours * 1e3:.1f} us ({pts / t_ours / 1e6:.0f} GPt/s), "
           f"speed-up {t_ref / t_ours:.2f}x")
+    _record(kernel="stencil", reference="v2 launch_stencil (mma.sync)", dtype="float16", shape=[H, W],
+            reference_us=t_ref * 1e3, pla_b200_us=t_ours * 1e3, speedup=t_ref / t_ours)
+    assert t_ours <= t_ref, f"pla_b200 {t_ours * 1e3:.1f} us slower than v2 {t_ref * 1e3:.1f} us"
 
 
 # ---------------------------------------------------------------------------
@@ -194,6 +211,7 @@ def test_against_reference_cutlass_depthwise(shape, dtype):
     pts = N * C * H * W
     t_ours = _time(ours)
     line = f"\n[depthwise {str(dtype)[6:]} {N}x{C}x{H}x{W}] pla_b200 {t_ours * 1e3:.1f} us ({pts / t_ours / 1e6:.0f} GPt/s)"
+    refs = {}
     for tag in ("v1", "v5", "v6"):
         launch = _dw(tag)
         y_ref = torch.empty_like(x)
@@ -205,5 +223,10 @@ def test_against_reference_cutlass_depthwise(shape, dtype):
         torch.cuda.synchronize()
         torch.testing.assert_close(y_ref.float().cpu(), want.to(dtype).float(), atol=tol, rtol=tol)
         t_ref = _time(ref)
+        refs[tag] = t_ref * 1e3
         line += f"; ref {tag} {t_ref * 1e3:.1f} us ({t_ref / t_ours:.2f}x)"
     print(line)
+    _record(kernel="depthwise", reference="CUTLASS v1/v5/v6 launch_depthwise_7x7_cutlass", dtype=str(dtype)[6:],
+            shape=list(shape), reference_us=refs, pla_b200_us=t_ours * 1e3,
+            speedup=min(refs.values()) / (t_ours * 1e3))
+    assert t_ours * 1e3 <= min(refs.values()), f"pla_b200 {t_ours * 1e3:.1f} us slower than {refs}"
