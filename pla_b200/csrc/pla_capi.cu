@@ -588,7 +588,10 @@ int launch_stack(const void* x, const void* w, const void* b, void* y, int dtype
   st = kernel_setup<stack_kernel<T, NHWC, S>>(G::THREADS, M::TOTAL, &per_sm);
   if (st != PLA_OK) return st;
   const long long slots = static_cast<long long>(d->sms) * per_sm;
-  const int grid = static_cast<int>(stages < slots ? stages : slots);
+  // Work units: stages, or half stages (kStackHalves, see stack_kernel.cuh).
+  const long long units = kStackHalves<T, S, false> ? 2 * stages : stages;
+  if (units > 0x7fffffffll) return PLA_ERR_TOO_LARGE;
+  const int grid = static_cast<int>(units < slots ? units : slots);
   stack_kernel<T, NHWC, S><<<grid, G::THREADS, M::TOTAL, stream>>>(xmap, ymap, a);
   PLA_CUDA(cudaGetLastError());
   return PLA_OK;
