@@ -74,7 +74,7 @@ PLA_API const char* pla_status_string(int status);
 PLA_API const char* pla_last_cuda_error(void);
 
 /* Library ABI version: (major << 16) | minor.  1.1 added pla_depthwise_forward,
- * 1.2 pla_depthwise7x7_layernorm_nhwc. */
+ * 1.2 pla_depthwise7x7_layernorm_nhwc, 1.3 pla_depthwise7x7_forward_many. */
 PLA_API int pla_version(void);
 
 /*
@@ -147,6 +147,34 @@ PLA_API int pla_depthwise7x7_forward(const void* x, const void* w, const void* b
 PLA_API int pla_depthwise_forward(const void* x, const void* w, const void* b, void* y,
                                   int n, int c, int h, int width, int k,
                                   int dtype, int layout, pla_stream_t stream);
+
+/*
+ * Several independent depthwise 7x7 problems in one call, for instance the
+ * four stages of the ConvNeXt-T-shaped sweep (data/depthwise_conv_7x7.py's
+ * benchmark shapes, one launcher call each in the reference,
+ * model_cutlass_autotune_v6.py:428-458).  Problem i is
+ * pla_depthwise7x7_forward(p[i].x, p[i].w, p[i].b, p[i].y, p[i].n, p[i].c,
+ * p[i].h, p[i].width, dtype, layout): same arguments and results.
+ *
+ * The problems run concurrently: the call forks from `stream` onto up to 4
+ * streams of the library (created once per device, on the first call made
+ * with that device current), launches the problems round-robin and joins
+ * back, so one problem's first tiles overlap another's last ones instead of
+ * each launch paying its own ramp and drain.  Work queued on `stream` before
+ * the call is finished before any problem starts; work queued after it
+ * starts after every problem is done.  No problem's output may overlap any
+ * problem's input or output (PLA_ERR_INVALID_ARGUMENT).  Arguments are
+ * checked for every problem before anything is launched.
+ */
+typedef struct pla_dw_problem {
+  const void* x;
+  const void* w;
+  const void* b; /* NULL: no bias */
+  void* y;
+  int n, c, h, width;
+} pla_dw_problem;
+PLA_API int pla_depthwise7x7_forward_many(const pla_dw_problem* problems, int count, int dtype, int layout,
+                                          pla_stream_t stream);
 
 /*
  * Depthwise 7x7 followed by LayerNorm over the channels of every pixel, in

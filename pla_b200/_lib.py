@@ -37,6 +37,7 @@ SIGNATURES = {
     "pla_stencil7x7_forward_taps": ([_vp, _f32p, _f32p, _vp, _i32, _i32, _i32, _i64, _i64, _i64, _i32, _vp], _i32),
     "pla_depthwise7x7_forward": ([_vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _i32, _vp], _i32),
     "pla_depthwise_forward": ([_vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _vp], _i32),
+    "pla_depthwise7x7_forward_many": ([_vp, _i32, _i32, _i32, _vp], _i32),
     "pla_depthwise7x7_layernorm_nhwc": ([_vp, _vp, _vp, _vp, _vp, ctypes.c_float, _vp, _i32, _i32, _i32, _i32, _i32,
                                          _vp], _i32),
     "pla_stencil7x7_iterate": ([_vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _vp], _i32),
@@ -52,6 +53,13 @@ SIGNATURES = {
     "pla_read_device_faults": ([_u32p], _i32),
     "pla_clear_device_faults": ([], _i32),
 }
+
+class DwProblem(ctypes.Structure):
+    """pla_dw_problem (include/pla_b200.h): one problem of pla_depthwise7x7_forward_many."""
+
+    _fields_ = [("x", ctypes.c_void_p), ("w", ctypes.c_void_p), ("b", ctypes.c_void_p), ("y", ctypes.c_void_p),
+                ("n", ctypes.c_int), ("c", ctypes.c_int), ("h", ctypes.c_int), ("width", ctypes.c_int)]
+
 
 _lib = None
 
@@ -70,7 +78,11 @@ def lib() -> ctypes.CDLL:
                 "this package has no CPU fallback")
         handle = ctypes.CDLL(LIB_PATH)
         for name, (argtypes, restype) in SIGNATURES.items():
-            fn = getattr(handle, name)
+            try:
+                fn = getattr(handle, name)
+            except AttributeError:
+                raise ImportError(f"{LIB_PATH} does not export {name}: it is older than the package; "
+                                  "rebuild it (python -m pla_b200.build)") from None
             fn.argtypes = argtypes
             fn.restype = restype
         _lib = handle

@@ -967,6 +967,55 @@ int noalloc_scratch(void** out) {
   return PLA_OK;
 }
 
+// ---- concurrent independent problems: fork / join over library streams ----
+constexpr int kForkStreams = 4;
+
+struct ForkJoin {
+  std::mutex mu;  // one call at a time per device: the events are reused
+  bool ready = false;
+  cudaStream_t s[kForkStreams];
+  cudaEvent_t fork, done[kForkStreams];
+};
+ForkJoin g_fork[kMaxDevices];
+
+// Creates the device's streams and events once (called with f.mu held, the
+// device current).  A failure leaves nothing behind, so a later call retries.
+int fork_join_setup(ForkJoin& f) {
+  if (f.ready) return PLA_OK;
+  cudaStream_t st[kForkStreams] = {};
+  cudaEvent_t ev[kForkStreams + 1] = {};
+  cudaError_t e = cudaSuccess;
+  for (int i = 0; i < kForkStreams && e == cudaSuccess; ++i)
+    e = cudaStreamCreateWithFlags(&st[i], cudaStreamNonBlocking);
+  for (int i = 0; i <= kForkStreams && e == cudaSuccess; ++i)
+    e = cudaEventCreateWithFlags(&ev[i], cudaEventDisableTiming);
+  if (e != cudaSuccess) {
+    for (cudaEvent_t x : ev)
+      if (x) cudaEventDestroy(x);
+    for (cudaStream_t x : st)
+      if (x) cudaStreamDestroy(x);
+    return cuda_fail(e, "fork/join stream setup");
+  }
+  for (int i = 0; i < kForkStreams; ++i) {
+    f.s[i] = st[i];
+    f.done[i] = ev[i];
+  }
+  f.fork = ev[kForkStreams];
+  f.ready = true;
+  return PLA_OK;
+}
+
+// Argument checks of pla_depthwise7x7_forward that need no device.
+int dw_check(const void* x, const void* w, const void* y, int n, int c, int h, int width, int dtype, int layout) {
+  if (!valid_dtype(dtype)) return PLA_ERR_UNSUPPORTED;
+  if (layout != PLA_NCHW && layout != PLA_NHWC) return PLA_ERR_INVALID_ARGUMENT;
+  if (n < 0 || c < 0 || h < 0 || width < 0) return PLA_ERR_INVALID_ARGUMENT;
+  if (static_cast<long long>(n) * c * h * width == 0) return PLA_OK;
+  if (!x || !w || !y) return PLA_ERR_INVALID_ARGUMENT;
+  if (h > (1 << 30) || width > (1 << 30)) return PLA_ERR_TOO_LARGE;
+  return PLA_OK;
+}
+
 }  // namespace
 }  // namespace pla
 
@@ -989,8 +1038,9 @@ const char* pla_status_string(int status) {
 
 const char* pla_last_cuda_error(void) { return g_last_cuda_error; }
 
-// 1.1: pla_depthwise_forward (k x k); 1.2: pla_depthwise7x7_layernorm_nhwc
-int pla_version(void) { return (1 << 16) | 2; }
+// 1.1: pla_depthwise_forward (k x k); 1.2: pla_depthwise7x7_layernorm_nhwc;
+// 1.3: pla_depthwise7x7_forward_many
+int pla_version(void) { return (1 << 16) | 3; }
 
 int pla_stencil7x7_forward(const void* x, const void* w, const void* b, void* y, int n, int h, int width,
                            int64_t sn, int64_t sh, int64_t sw, int dtype, pla_stream_t stream) {
@@ -1052,6 +1102,56 @@ int pla_depthwise7x7_forward(const void* x, const void* w, const void* b, void* 
   a.total = planes * plane;
   a.K = 7;
   return launch_generic_dtype(dtype, a, s);
+}
+
+int pla_depthwise7x7_forward_many(const pla_dw_problem* p, int count, int dtype, int layout, pla_stream_t stream) {
+  if (count < 0 || (count > 0 && !p) || count > 1024) return PLA_ERR_INVALID_ARGUMENT;
+  const size_t es = dtype_size(dtype);
+  for (int i = 0; i < count; ++i) {
+    const int st = dw_check(p[i].x, p[i].w, p[i].y, p[i].n, p[i].c, p[i].h, p[i].width, dtype, layout);
+    if (st != PLA_OK) return st;
+  }
+  // No output may overlap any input or output of the call (the problems run
+  // concurrently).
+  for (int i = 0; i < count; ++i) {
+    const long long ei = static_cast<long long>(p[i].n) * p[i].c * p[i].h * p[i].width;
+    if (ei == 0) continue;
+    const Span yi = dense_span(p[i].y, ei, es);
+    for (int j = 0; j < count; ++j) {
+      const long long ej = static_cast<long long>(p[j].n) * p[j].c * p[j].h * p[j].width;
+      if (ej == 0) continue;
+      if (overlap(yi, dense_span(p[j].x, ej, es))) return PLA_ERR_INVALID_ARGUMENT;
+      if (j != i && overlap(yi, dense_span(p[j].y, ej, es))) return PLA_ERR_INVALID_ARGUMENT;
+    }
+  }
+  if (count == 0) return PLA_OK;
+  if (count == 1)
+    return pla_depthwise7x7_forward(p[0].x, p[0].w, p[0].b, p[0].y, p[0].n, p[0].c, p[0].h, p[0].width, dtype,
+                                    layout, stream);
+  int dev;
+  int st = current_device(&dev);
+  if (st != PLA_OK) return st;
+  ForkJoin& f = g_fork[dev];
+  std::lock_guard<std::mutex> lock(f.mu);
+  st = fork_join_setup(f);
+  if (st != PLA_OK) return st;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int used = count < kForkStreams ? count : kForkStreams;
+  PLA_CUDA(cudaEventRecord(f.fork, s));
+  for (int i = 0; i < used; ++i) PLA_CUDA(cudaStreamWaitEvent(f.s[i], f.fork, 0));
+  int first_err = PLA_OK;
+  for (int i = 0; i < count; ++i) {
+    const int r = pla_depthwise7x7_forward(p[i].x, p[i].w, p[i].b, p[i].y, p[i].n, p[i].c, p[i].h, p[i].width,
+                                           dtype, layout, reinterpret_cast<pla_stream_t>(f.s[i % used]));
+    if (r != PLA_OK && first_err == PLA_OK) first_err = r;
+  }
+  // Join every forked stream back, also after a failed launch, so the
+  // caller's stream never runs ahead of work this call queued.
+  for (int i = 0; i < used; ++i) {
+    PLA_CUDA(cudaEventRecord(f.done[i], f.s[i]));
+    PLA_CUDA(cudaStreamWaitEvent(s, f.done[i], 0));
+  }
+  return first_err;
 }
 
 int pla_depthwise_forward(const void* x, const void* w, const void* b, void* y, int n, int c, int h, int width,

@@ -99,6 +99,60 @@ def depthwise_kxk(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | No
     return out
 
 
+def depthwise7x7_many(problems, outs=None) -> list[torch.Tensor]:
+    """Several independent 7x7 depthwise convolutions in one call, run
+    concurrently (``pla_depthwise7x7_forward_many``): ``problems`` is a list of
+    ``(x, weight, bias_or_None)`` CUDA tensors of one dtype and one layout
+    (all contiguous NCHW or all channels_last), e.g. the four stages of a
+    ConvNeXt-T-shaped sweep.  Returns the outputs in order, in x's memory
+    format (or writes into ``outs``).  Each result equals
+    ``depthwise7x7(x, weight, bias)`` bit for bit.
+    """
+    problems = list(problems)
+    if not problems:
+        return []
+    x0 = problems[0][0]
+    if not isinstance(x0, torch.Tensor) or not x0.is_cuda:
+        raise ValueError("depthwise7x7_many requires CUDA inputs")
+    if x0.dtype not in _lib.DTYPE_CODE:
+        raise RuntimeError("unsupported dtype")
+    if x0.dim() == 4 and x0.is_contiguous():
+        layout, fmt = _lib.PLA_NCHW, torch.contiguous_format
+    elif x0.dim() == 4 and x0.is_contiguous(memory_format=torch.channels_last):
+        layout, fmt = _lib.PLA_NHWC, torch.channels_last
+    else:
+        raise RuntimeError("depthwise7x7_many takes dense NCHW or channels_last [N,C,H,W] inputs")
+    arr = (_lib.DwProblem * len(problems))()
+    keep = []
+    results = []
+    for i, (x, w, b) in enumerate(problems):
+        if not isinstance(x, torch.Tensor) or not x.is_cuda or x.device != x0.device or x.dtype != x0.dtype:
+            raise RuntimeError("every problem's input must be a CUDA tensor of the first one's device and dtype")
+        if x.dim() != 4 or not x.is_contiguous(memory_format=fmt):
+            raise RuntimeError("every problem's input must have the first one's layout")
+        N, C, H, W = x.shape
+        if not w.is_cuda or w.device != x.device or w.dtype != x.dtype or w.numel() != C * 49:
+            raise RuntimeError("weight must be a [C,1,7,7] CUDA tensor of x's dtype on x's device")
+        if b is not None and (not b.is_cuda or b.device != x.device or b.dtype != x.dtype or b.numel() != C):
+            raise RuntimeError("bias device/dtype/shape mismatch")
+        if outs is None:
+            y = torch.empty(x.shape, dtype=x.dtype, device=x.device, memory_format=fmt)
+        else:
+            y = outs[i]
+            if y.shape != x.shape or y.dtype != x.dtype or not y.is_contiguous(memory_format=fmt):
+                raise RuntimeError("out must match x's shape, dtype and memory format")
+        w = w.detach().contiguous()
+        b = None if b is None else b.detach().contiguous()
+        keep += [w, b]
+        arr[i] = _lib.DwProblem(x.data_ptr(), w.data_ptr(), _lib.ptr(b), y.data_ptr(), N, C, H, W)
+        results.append(y)
+    with torch.cuda.device(x0.device):
+        st = _lib.lib().pla_depthwise7x7_forward_many(arr, len(problems), _lib.DTYPE_CODE[x0.dtype], layout,
+                                                      _lib.stream_ptr(x0.device))
+    _lib.check(st, "pla_depthwise7x7_forward_many")
+    return results
+
+
 def depthwise7x7_layernorm(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None,
                            norm_weight: torch.Tensor | None = None, norm_bias: torch.Tensor | None = None,
                            eps: float = 1e-6, out: torch.Tensor | None = None) -> torch.Tensor:

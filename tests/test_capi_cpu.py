@@ -265,3 +265,28 @@ def test_overlapping_buffers_are_rejected_before_any_device_work():
     flags = (ctypes.c_uint * 2)()
     assert L.pla_stencil7x7_band_step_halo(base, taps, None, base + 256, 64, 32, F32, None, 0, None, flags, None,
                                            None, flags, 0, None) == 1
+
+
+def test_many_rejects_bad_batches_before_any_device_work():
+    """pla_depthwise7x7_forward_many checks every problem, and that no output
+    overlaps any problem's input or output, before it touches a device."""
+    from pla_b200 import _lib
+
+    L = _lib.lib()
+    F32 = _lib.PLA_F32
+    P = _lib.DwProblem
+    base = 1 << 20
+    arr = (P * 2)(P(base, base + (1 << 19), None, base + (1 << 18), 1, 4, 8, 8),
+                  P(base + (1 << 17), base + (1 << 19), None, base + (1 << 18) + 64, 1, 4, 8, 8))
+    assert L.pla_depthwise7x7_forward_many(arr, 2, F32, _lib.PLA_NCHW, None) == 1   # the two outputs overlap
+    arr[1].y = base + (1 << 17) + 16                                               # output 1 inside input 1
+    assert L.pla_depthwise7x7_forward_many(arr, 2, F32, _lib.PLA_NCHW, None) == 1
+    arr[1].y = base + 32                                                            # output 1 inside input 0
+    assert L.pla_depthwise7x7_forward_many(arr, 2, F32, _lib.PLA_NCHW, None) == 1
+    arr[1].n = -1
+    assert L.pla_depthwise7x7_forward_many(arr, 2, F32, _lib.PLA_NCHW, None) == 1
+    assert L.pla_depthwise7x7_forward_many(arr, -1, F32, _lib.PLA_NCHW, None) == 1
+    assert L.pla_depthwise7x7_forward_many(None, 2, F32, _lib.PLA_NCHW, None) == 1
+    assert L.pla_depthwise7x7_forward_many(arr, 2, 9, _lib.PLA_NCHW, None) == 2
+    assert L.pla_depthwise7x7_forward_many(arr, 2, F32, 7, None) == 1
+    assert L.pla_depthwise7x7_forward_many(None, 0, F32, _lib.PLA_NCHW, None) == 0
