@@ -69,5 +69,7 @@ def test_many_in_a_cuda_graph_and_on_a_side_stream():
 def test_many_rejects_an_output_that_is_another_problems_input():
     probs = _problems(1, torch.float32, torch.contiguous_format, 33, bias=False)
     args = [(xd, wd, bd) for (_, _, _, xd, wd, bd) in probs[:2]]
-    with pytest.raises(RuntimeError):
-        depthwise7x7_many(args, outs=[torch.empty_like(args[0][0]), args[0][0].view_as(args[0][0])])
+    x0, x1 = args[0][0], args[1][0]
+    inside_x0 = x0.view(-1)[:x1.numel()].view(x1.shape)  # problem 1's output inside problem 0's input
+    with pytest.raises(RuntimeError, match="invalid argument"):
+        depthwise7x7_many(args, outs=[torch.empty_like(x0), inside_x0])
