@@ -375,6 +375,8 @@ class DepthwiseBase:
     def rebind(self, stream_ptr):
         """Launch the bound calls on another stream (the CUDA-graph capture stream)."""
         self._args = [[a[:-1] + (stream_ptr,) for a in per] for per in self._args]
+        if self.concurrent:
+            self._bind_many(stream_ptr)
 
     _stage_events = None
 
@@ -395,8 +397,28 @@ class DepthwiseBase:
         evs, self._stage_events = self._stage_events, None
         return sum(a.elapsed_time(b) for a, b in evs) / len(evs)
 
+    concurrent = False  # True: a step is one pla_depthwise7x7_forward_many call over all stages
+
+    def _bind_many(self, stream_ptr):
+        from pla_b200 import _lib
+
+        code = _lib.DTYPE_CODE[self.torch_dtype]
+        lay = _lib.PLA_NHWC if self.layout == "nhwc" else _lib.PLA_NCHW
+        self._many = []
+        for per in self._args:
+            arr = (_lib.DwProblem * len(per))()
+            for j, a in enumerate(per):
+                arr[j] = _lib.DwProblem(a[0], a[1], a[2], a[3], a[4], a[5], a[6], a[7])
+            self._many.append((arr, len(per), code, lay, stream_ptr))
+        self._many_call = _lib.lib().pla_depthwise7x7_forward_many
+
     def step(self, i):
         evs = self._stage_events
+        if self.concurrent and evs is None:
+            st = self._many_call(*self._many[i % self.nsets])
+            if st:
+                raise RuntimeError(f"pla_depthwise7x7_forward_many failed: {st}")
+            return
         for j, args in enumerate(self._args[i % self.nsets]):
             if evs is not None and j == self._dom:
                 evs[self._stage_n][0].record()
@@ -408,9 +430,13 @@ class DepthwiseBase:
                 self._stage_n += 1
 
     def config(self):
-        return {"workload": self.name, "stages": [list(s) for s in self.stages], "layout": self.layout,
-                "bias": self.bias, "seed": self.seed, "x": "N(0,1)", "w": "N(0,1/49)",
-                "l2": f"inputs rotate over {self.nsets} buffer sets", "parallelism": self.parallelism}
+        c = {"workload": self.name, "stages": [list(s) for s in self.stages], "layout": self.layout,
+             "bias": self.bias, "seed": self.seed, "x": "N(0,1)", "w": "N(0,1/49)",
+             "l2": f"inputs rotate over {self.nsets} buffer sets", "parallelism": self.parallelism}
+        if self.concurrent:
+            c["stream_pass"] = "stages one after another on one stream, the largest bracketed by CUDA events " \
+                               "(roofline of that kernel)"
+        return c
 
     parallelism = "one batch per GPU (replicas, no collective)"
 
@@ -436,7 +462,12 @@ class DepthwiseBase:
             s_cmp.wait_event(ev["in_done"][k])
             if ev["out_done"][k] is not None:
                 s_cmp.wait_event(ev["out_done"][k])
-            ys = [self._fn(d, w, b) for d, (_, _, w, b) in zip(self.dx[k], self.dev_items)]
+            if self.concurrent:
+                from pla_b200.depthwise import depthwise7x7_many
+
+                ys = depthwise7x7_many([(d, w, b) for d, (_, _, w, b) in zip(self.dx[k], self.dev_items)])
+            else:
+                ys = [self._fn(d, w, b) for d, (_, _, w, b) in zip(self.dx[k], self.dev_items)]
             ev["cmp_done"][k] = torch.cuda.Event()
             ev["cmp_done"][k].record(s_cmp)
         with torch.cuda.stream(s_out):
@@ -526,7 +557,14 @@ class DwCfg4(DepthwiseBase):
     bias = False
     seed = 3
     scaling = "strong"
-    parallelism = "batch sharded over GPUs (N/world images per GPU), no collective"
+    parallelism = "batch sharded over GPUs (N/world images per GPU), no collective; the four stages of a step " \
+                  "run concurrently in one pla_depthwise7x7_forward_many call"
+    concurrent = True
+
+    def __init__(self, rank, world, dev):
+        super().__init__(rank, world, dev)
+        if dev is not None and self.concurrent:
+            self._bind_many(torch.cuda.current_stream(dev).cuda_stream)
 
     @staticmethod
     def local_batch(N, world, rank):
@@ -551,6 +589,8 @@ class DwLnCfg4(DwCfg4):
     name = "depthwise7x7_layernorm_cfg4_convnext_t_N256_bf16_nhwc"
     layout = "nhwc"
     ln_params = 2  # scale and shift: C elements each
+    concurrent = False
+    parallelism = "batch sharded over GPUs (N/world images per GPU), no collective"
 
     def __init__(self, rank, world, dev):
         super().__init__(rank, world, dev)
