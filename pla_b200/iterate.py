@@ -342,3 +342,124 @@ class BandedStencil:
     def run(self, steps: int) -> None:
         for _ in range(steps):
             self.step()
+
+    # -- one whole job with the transfers overlapped (single band) -----------
+    @staticmethod
+    def job_schedule(rows: int, steps: int, chunks: int, max_skew: int = 48):
+        """Row-range launches of ``run_job`` on one band of ``rows`` rows.
+
+        Returns ``(edges, k, launches)``: chunk edges e_0 < ... < e_{C-1} = rows
+        (band rows), the number k of skewed steps at each end, and the launch
+        list of (kind, chunk, step, row_begin, row_end) with kind "in" (wait for
+        chunk c's input copy), "step", "out" (copy chunk c's final rows) in
+        issue order.
+
+        Steps 1..k run chunk by chunk as each chunk's input arrives: chunk c
+        of step s ends 3 s rows above the chunk's end e_c (its rows' 7x7 cone
+        over s steps stays inside the rows already copied; the last chunk
+        ends at the band's end).  Steps k+1..steps-k run whole.  Steps
+        steps-k+1..steps run chunk by chunk again, chunk c of step s ending
+        3 (steps - s) rows past e_c, so chunk c's final rows [e_{c-1}, e_c)
+        are done, and copied out, while later chunks still compute.  In both
+        skewed phases a launch only overwrites rows that no later launch of
+        an earlier step reads (the regions of consecutive steps meet without
+        overlapping), so two ping-pong buffers suffice.
+        """
+        C = max(1, min(chunks, rows // 8))
+        edges = [(rows * (c + 1)) // C for c in range(C)]
+        height = min(b - a for a, b in zip([0] + edges[:-1], edges))
+        k = max(0, min(steps // 2, (height - 1) // 3, max_skew)) if C > 1 else 0
+        L = []
+
+        def hi_in(c, st):
+            return rows if c == C - 1 else edges[c] - 3 * st
+
+        def hi_out(c, st):
+            return rows if c == C - 1 else min(rows, edges[c] + 3 * (steps - st))
+
+        for c in range(C):
+            L.append(("in", c, 0, 0, 0))
+            for st in range(1, k + 1):
+                lo = 0 if c == 0 else hi_in(c - 1, st)
+                L.append(("step", c, st, lo, hi_in(c, st)))
+        for st in range(k + 1, steps - k + 1):
+            L.append(("step", -1, st, 0, rows))
+        if k == 0:  # no skew: the output of the last whole step, chunk by chunk
+            for c in range(C):
+                L.append(("out", c, steps, 0, 0))
+            return edges, k, L
+        for c in range(C):
+            for st in range(steps - k + 1, steps + 1):
+                lo = 0 if c == 0 else hi_out(c - 1, st)
+                L.append(("step", c, st, lo, hi_out(c, st)))
+            L.append(("out", c, steps, 0, 0))
+        return edges, k, L
+
+    def run_job(self, host_rows: torch.Tensor, row0: int, steps: int, host_out: torch.Tensor,
+                chunks: int = 16) -> None:
+        """One whole job through this band: its rows from ``host_rows`` (pinned
+        host memory holding grid rows [row0, ...)), ``steps`` steps, the band's
+        final rows into ``host_out`` ([rows, W], pinned), stream-ordered on the
+        current stream.
+
+        One band (world size 1, zero halos left by ``load``): the copies run on
+        a side stream in ``chunks`` row chunks and overlap the steps
+        (``job_schedule``): the first steps start on the rows already copied
+        in, the last ones finish the top chunks first, which are copied out
+        while the rest compute.  Same results bit for bit as copy-in, ``run``,
+        copy-out.  Several bands (p2p or NCCL exchange): copy in, ``run``,
+        copy out, in order.
+        """
+        if self.world > 1 or host_out.shape != (self.rows, self.W):
+            if host_out.shape != (self.rows, self.W):
+                raise ValueError("host_out must be [rows, W]")
+            self.load_async(host_rows, row0)
+            self.run(steps)
+            host_out.copy_(self.band(), non_blocking=True)
+            return
+        a0, a1 = self.halo_span()
+        if row0 > a0 or row0 + host_rows.shape[0] < a1:
+            raise ValueError("host rows do not cover the band")
+        R = self.rows
+        edges, k, launches = self.job_schedule(R, steps, chunks)
+        cur0 = self.cur
+        cuda = self.device.type == "cuda"
+        comp = torch.cuda.current_stream(self.device) if cuda else None
+        copy = self.comm_stream
+        if cuda:
+            copy.wait_stream(comp)
+        ev_in, ev_out = {}, {}
+        prev = 0
+        # every input chunk is queued on the copy stream at once; the steps wait per chunk
+        for c, e in enumerate(edges):
+            src = host_rows[prev - row0 + self.r0:e - row0 + self.r0]
+            dst = self.bufs[cur0][3 + prev:3 + e]
+            if cuda:
+                with torch.cuda.stream(copy):
+                    dst.copy_(src, non_blocking=True)
+                    ev_in[c] = torch.cuda.Event()
+                    ev_in[c].record(copy)
+            else:
+                dst.copy_(src)
+            prev = e
+        for kind, c, st, lo, hi in launches:
+            if kind == "in":
+                if cuda:
+                    comp.wait_event(ev_in[c])
+            elif kind == "step":
+                if hi > lo:
+                    self.step_fn(self.bufs[(cur0 + st - 1) % 2], self.bufs[(cur0 + st) % 2], lo, hi)
+            else:  # out: chunk c's final rows
+                lo_r = 0 if c == 0 else edges[c - 1]
+                src = self.bufs[(cur0 + st) % 2][3 + lo_r:3 + edges[c]]
+                if cuda:
+                    ev_out[c] = torch.cuda.Event()
+                    ev_out[c].record(comp)
+                    copy.wait_event(ev_out[c])
+                    with torch.cuda.stream(copy):
+                        host_out[lo_r:edges[c]].copy_(src, non_blocking=True)
+                else:
+                    host_out[lo_r:edges[c]].copy_(src)
+        if cuda:
+            comp.wait_stream(copy)
+        self.cur = (cur0 + steps) % 2

@@ -163,3 +163,67 @@ def test_rank_leaving_raises_on_the_survivor():
     for p in procs:
         p.join(timeout=60)
     assert outcome != "no error"
+
+
+# ---- the overlapped whole-job schedule of one band ------------------------------
+@pytest.mark.parametrize("rows,steps,chunks", [(96, 10, 4), (200, 7, 16), (64, 2, 8), (130, 30, 5), (40, 1, 4)])
+def test_job_schedule_covers_every_step_once(rows, steps, chunks):
+    from pla_b200.iterate import BandedStencil
+
+    edges, k, launches = BandedStencil.job_schedule(rows, steps, chunks)
+    assert edges[-1] == rows and all(a < b for a, b in zip([0] + edges[:-1], edges))
+    assert 2 * k <= steps
+    covered = {st: [] for st in range(1, steps + 1)}
+    arrived = set()
+    done_out = set()
+    lo_of = [0] + edges[:-1]
+    for kind, c, st, lo, hi in launches:
+        if kind == "in":
+            arrived.add(c)
+        elif kind == "step":
+            assert 0 <= lo <= hi <= rows
+            covered[st].append((lo, hi))
+            if hi > lo and st % 2 == 0:  # writes the input buffer: never rows still being copied in
+                for p in set(range(len(edges))) - arrived:
+                    assert hi <= lo_of[p] or lo >= edges[p]
+            if hi > lo and st % 2 == steps % 2:  # writes the output buffer: never rows being copied out
+                for p in done_out:
+                    assert hi <= lo_of[p] or lo >= edges[p]
+            if st == 1:  # the rows read (lo - 3 .. hi + 3) have been copied in
+                need = hi + 3
+                got = max([edges[a] for a in arrived], default=0)
+                assert need <= got or hi == rows and max(arrived) == len(edges) - 1
+        else:
+            done_out.add(c)
+            # chunk c's final rows are complete before they are copied out
+            lo_r = 0 if c == 0 else edges[c - 1]
+            fin = sorted(covered[steps])
+            assert any(a <= lo_r and edges[c] <= b for a, b in fin) or \
+                sum(min(b, edges[c]) - max(a, lo_r) for a, b in fin if b > lo_r and a < edges[c]) == edges[c] - lo_r
+    assert done_out == set(range(len(edges)))
+    for st, regs in covered.items():
+        regs = sorted(r for r in regs if r[1] > r[0])
+        assert regs[0][0] == 0 and regs[-1][1] == rows
+        assert all(a[1] == b[0] for a, b in zip(regs, regs[1:]))  # contiguous, no overlap
+
+
+@pytest.mark.parametrize("rows,steps,chunks", [(96, 10, 4), (130, 30, 5), (64, 2, 8), (40, 1, 4)])
+def test_run_job_matches_the_oracle_iteration(rows, steps, chunks):
+    """run_job (copy in by chunks, skewed first and last steps, copy out by
+    chunks) equals the plain oracle iteration bit for bit, and leaves the band
+    ready for the next job."""
+    from pla_b200.iterate import BandedStencil
+
+    W = 24
+    g = torch.Generator().manual_seed(9)
+    x = torch.rand(rows, W, generator=g) * 2 - 1
+    w = torch.rand(7, 7, generator=g) * 2 - 1
+    w = w / w.sum()
+    bs = BandedStencil(rows, W, w, device=torch.device("cpu"), step_fn=_oracle_band_step(w))
+    bs.load(torch.zeros(rows, W))
+    out = torch.empty(rows, W)
+    bs.run_job(x, 0, steps, out, chunks=chunks)
+    assert torch.equal(out, oracle.stencil7x7_iterate(x, w, steps))
+    x2 = torch.rand(rows, W, generator=g)
+    bs.run_job(x2, 0, steps + 1, out, chunks=chunks)
+    assert torch.equal(out, oracle.stencil7x7_iterate(x2, w, steps + 1))
