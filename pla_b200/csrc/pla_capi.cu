@@ -130,6 +130,26 @@ Span strided_span(const void* p, size_t es, int nd, const long long* ext, const 
 }
 bool overlap(Span a, Span b) { return a.lo < b.hi && b.lo < a.hi; }
 
+// Launch with programmatic dependent launch allowed: the kernel may start
+// (CTA launch, barrier init, tensor-map prefetch) while the previous kernel
+// in the stream drains; it waits for that kernel's completion and memory
+// flush (griddepcontrol.wait) before touching global memory.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), int grid, int threads, uint32_t smem, cudaStream_t stream,
+                       Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(threads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 // Per-(kernel, device) one-time attribute setup (dynamic smem opt-in) and
 // the resident-CTA count used to size persistent grids.
 template <auto Kernel>
@@ -259,14 +279,16 @@ int launch_tile(const void* x, const void* w, const void* b, const HostTaps* ht,
   const HaloLinks no_halo{};
   if constexpr (K == 7) {
     if (ht) {
-      tile_kernel<T, R, LX, true><<<grid, kTileThreads, G::SMEM, stream>>>(map, a, *ht, no_halo);
+      PLA_CUDA(launch_pdl(tile_kernel<T, R, LX, true>, grid, kTileThreads, G::SMEM, stream, map, a, *ht, no_halo));
     } else {
       HostTaps unused{};
-      tile_kernel<T, R, LX, false><<<grid, kTileThreads, G::SMEM, stream>>>(map, a, unused, no_halo);
+      PLA_CUDA(launch_pdl(tile_kernel<T, R, LX, false>, grid, kTileThreads, G::SMEM, stream, map, a, unused,
+                          no_halo));
     }
   } else {
     HostTaps unused{};
-    tile_kernel<T, R, LX, false, false, K><<<grid, kTileThreads, G::SMEM, stream>>>(map, a, unused, no_halo);
+    PLA_CUDA(launch_pdl(tile_kernel<T, R, LX, false, false, K>, grid, kTileThreads, G::SMEM, stream, map, a, unused,
+                        no_halo));
   }
   PLA_CUDA(cudaGetLastError());
   return PLA_OK;
@@ -411,7 +433,8 @@ int launch_tile_halo(const void* in, const HostTaps& ht, void* out_rows, int dty
   // Static striding: tile claiming measured 0.6 % slower for the fused
   // halo step (2 GPUs, same box), unlike the plain band step.
   const int grid = static_cast<int>(total < slots ? total : slots);
-  tile_kernel<T, kWideR, kWideLX, true, true><<<grid, kTileThreads, G::SMEM, stream>>>(map, a, ht, links);
+  PLA_CUDA(launch_pdl(tile_kernel<T, kWideR, kWideLX, true, true>, grid, kTileThreads, G::SMEM, stream, map, a, ht,
+                      links));
   PLA_CUDA(cudaGetLastError());
   return PLA_OK;
 }

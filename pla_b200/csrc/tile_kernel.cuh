@@ -147,6 +147,10 @@ __global__ void __launch_bounds__(kTileThreads, HOST_TAPS ? 5 : 4)
     fence_mbar_init();
   }
   __syncthreads();
+  // Launched with programmatic dependent launch: everything above overlaps
+  // the previous kernel's drain; every global read or write below comes
+  // after that kernel has completed and flushed (a no-op otherwise).
+  grid_dependency_wait();
 
   const int total = a.total_tiles;
   const int stride = gridDim.x;
@@ -223,6 +227,7 @@ __global__ void __launch_bounds__(kTileThreads, HOST_TAPS ? 5 : 4)
           claim();
         } else {
           claiming = false;
+          launch_dependents();  // this CTA is on its last tile
         }
         next_tile[it & 1] = nt;  // read by every thread after this iteration's barrier
       }
@@ -230,6 +235,8 @@ __global__ void __launch_bounds__(kTileThreads, HOST_TAPS ? 5 : 4)
       // Tile it + NS - 1 goes into the stage that tile it - 1 used; every
       // thread left that stage at the barrier that ended iteration it - 1.
       issue(t + (NS - 1) * stride, (it + NS - 1) % NS);
+    } else if (tid == 0) {
+      launch_dependents();  // this CTA is on its last tile
     }
 
     const int q = fdiv(t, a.div_tx);
