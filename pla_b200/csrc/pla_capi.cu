@@ -150,6 +150,18 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), int grid, int threads, uint32_t
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
+// Tile-kernel launch: static-striding launches (persistent CTAs, at most a
+// few tiles each) with programmatic dependent launch, which measured 6.5 %
+// faster on back-to-back 4096^2 steps; tile-claiming launches (one CTA per
+// tile) without it: on a 32768^2 band step it measured 10 % slower.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_tile_kernel(void (*kernel)(KArgs...), bool pdl, int grid, uint32_t smem, cudaStream_t stream,
+                               Args&&... args) {
+  if (pdl) return launch_pdl(kernel, grid, kTileThreads, smem, stream, std::forward<Args>(args)...);
+  kernel<<<grid, kTileThreads, smem, stream>>>(std::forward<Args>(args)...);
+  return cudaGetLastError();
+}
+
 // Per-(kernel, device) one-time attribute setup (dynamic smem opt-in) and
 // the resident-CTA count used to size persistent grids.
 template <auto Kernel>
@@ -279,16 +291,16 @@ int launch_tile(const void* x, const void* w, const void* b, const HostTaps* ht,
   const HaloLinks no_halo{};
   if constexpr (K == 7) {
     if (ht) {
-      PLA_CUDA(launch_pdl(tile_kernel<T, R, LX, true>, grid, kTileThreads, G::SMEM, stream, map, a, *ht, no_halo));
+      PLA_CUDA(launch_tile_kernel(tile_kernel<T, R, LX, true>, !a.dyn, grid, G::SMEM, stream, map, a, *ht, no_halo));
     } else {
       HostTaps unused{};
-      PLA_CUDA(launch_pdl(tile_kernel<T, R, LX, false>, grid, kTileThreads, G::SMEM, stream, map, a, unused,
-                          no_halo));
+      PLA_CUDA(launch_tile_kernel(tile_kernel<T, R, LX, false>, !a.dyn, grid, G::SMEM, stream, map, a, unused,
+                                  no_halo));
     }
   } else {
     HostTaps unused{};
-    PLA_CUDA(launch_pdl(tile_kernel<T, R, LX, false, false, K>, grid, kTileThreads, G::SMEM, stream, map, a, unused,
-                        no_halo));
+    PLA_CUDA(launch_tile_kernel(tile_kernel<T, R, LX, false, false, K>, !a.dyn, grid, G::SMEM, stream, map, a,
+                                unused, no_halo));
   }
   PLA_CUDA(cudaGetLastError());
   return PLA_OK;
@@ -611,10 +623,7 @@ int launch_stack(const void* x, const void* w, const void* b, void* y, int dtype
   st = kernel_setup<stack_kernel<T, NHWC, S>>(G::THREADS, M::TOTAL, &per_sm);
   if (st != PLA_OK) return st;
   const long long slots = static_cast<long long>(d->sms) * per_sm;
-  // Work units: stages, or half stages (kStackHalves, see stack_kernel.cuh).
-  const long long units = kStackHalves<T, S, false> ? 2 * stages : stages;
-  if (units > 0x7fffffffll) return PLA_ERR_TOO_LARGE;
-  const int grid = static_cast<int>(units < slots ? units : slots);
+  const int grid = static_cast<int>(stages < slots ? stages : slots);
   stack_kernel<T, NHWC, S><<<grid, G::THREADS, M::TOTAL, stream>>>(xmap, ymap, a);
   PLA_CUDA(cudaGetLastError());
   return PLA_OK;

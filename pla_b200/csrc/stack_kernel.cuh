@@ -145,69 +145,13 @@ __device__ __forceinline__ float raw_to_f(float v) { return v; }
 __device__ __forceinline__ float raw_to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
 __device__ __forceinline__ float raw_to_f(__half v) { return __half2float(v); }
 
-// Half-stage work units (stack_kernel): 16-bit stacks of 14 x 14 and 28 x 28
-// planes without the LayerNorm epilogue.  Their warps own R = 2 rows, so a
-// half stage (S / 2 rows) is one row per warp.
-template <typename T, int S, bool LN>
-constexpr bool kStackHalves = kMixStack<T> && !LN && S != 7;
-
-// RR output rows from row y0 (rows at or past S are skipped) x S columns of
-// plane / channel `ln`, read straight from the raw 16-bit stage: 16-bit x and
-// w into mixed-precision FMAs (fp32 accumulator), taps in (ky, kx) order,
-// taps on the zero padding skipped.  acc must enter zeroed.
-template <typename T, bool NHWC, int S, int RR, int LANES>
-__device__ __forceinline__ void mix_rows(const T* rs, int ln, int y0, const uint32_t (&wh)[(kTaps + 1) / 2],
-                                         float (&acc)[RR][S]) {
-  constexpr int PLANE = S * S;
-  const unsigned short* r16 = reinterpret_cast<const unsigned short*>(rs);
-#pragma unroll
-  for (int ir = 0; ir < RR + 6; ++ir) {
-    const int iy = y0 + ir - kHalo;
-    if (iy < 0 || iy >= S) continue;  // zero-padding row (warp-uniform)
-    unsigned short xv[S];           // row iy of plane / channel ln
-    if constexpr (NHWC) {
-#pragma unroll
-      for (int xx = 0; xx < S; ++xx) xv[xx] = r16[(iy * S + xx) * LANES + ln];
-    } else if constexpr (S % 2 == 0) {
-      const uint32_t* p = reinterpret_cast<const uint32_t*>(r16 + ln * PLANE + iy * S);
-#pragma unroll
-      for (int q2 = 0; q2 < S / 2; ++q2) {
-        const uint32_t u = p[q2];
-        xv[2 * q2] = half_of(u, 0);
-        xv[2 * q2 + 1] = half_of(u, 1);
-      }
-    } else {  // odd-width rows are not word aligned
-#pragma unroll
-      for (int xx = 0; xx < S; ++xx) xv[xx] = r16[ln * PLANE + iy * S + xx];
-    }
-#pragma unroll
-    for (int kx = 0; kx < 7; ++kx) {
-#pragma unroll
-      for (int r = 0; r < RR; ++r) {
-        const int ky = ir - r;
-        if (ky < 0 || ky >= 7) continue;
-        const int k = ky * 7 + kx;
-        const unsigned short wv = half_of(wh[k >> 1], k & 1);
-#pragma unroll
-        for (int o = 0; o < S; ++o) {
-          const int ix = o + kx - kHalo;
-          if (ix < 0 || ix >= S) continue;  // zero-padding column (compile time)
-          acc[r][o] = fma_mix(T(), xv[ix], wv, acc[r][o]);
-        }
-      }
-    }
-  }
-}
-
 template <typename T, bool NHWC, int S, bool LN = false>
 __global__ void __launch_bounds__(StackGeom<S, kMixStack<T>>::THREADS, StackGeom<S, kMixStack<T>>::MIN_BLOCKS)
     stack_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap ymap,
                  const StackArgs a) {
   static_assert(!LN || NHWC, "the LayerNorm epilogue normalises the channels of NHWC pixels");
   constexpr bool MIX = kMixStack<T>;
-  constexpr bool HALVES = kStackHalves<T, S, LN>;
   using G = StackGeom<S, MIX>;
-  static_assert(!HALVES || (G::R == 2 && G::G == 1 && 2 * G::RG == S), "a half stage is one row per warp");
   using M = StackSmem<T, S, LN>;
   constexpr int R = G::R, Q = G::Q, LANES = G::LANES;
   extern __shared__ __align__(128) unsigned char smem[];
@@ -258,26 +202,13 @@ __global__ void __launch_bounds__(StackGeom<S, kMixStack<T>>::THREADS, StackGeom
   // cluster's balanced range of images, in this rank's channel group
   // (virtual stage = channel group * N + image); every rank of a cluster
   // runs the same number of stages.
-  // HALVES (16-bit stacks of 14 x 14 / 28 x 28 planes): the units handed out
-  // are half stages (rows [0, S/2) or [S/2, S) of the stage's planes), so a
-  // CTA's range may start or end in the middle of a stage.  A stage whose
-  // two halves are both in the range is computed whole (R rows per warp);
-  // a lone half is computed by every warp on one row.  With 3.5 stages per
-  // CTA this turns a last round that runs on half the CTAs into one that
-  // runs on all of them, at half the length.
   int v_begin, v_end;
-  int h_begin = 0, h_end = 0;  // HALVES: range of half units
   int rank = 0;
   if constexpr (LN) {
     rank = static_cast<int>(cluster_ctarank());
     const long long cid = cluster_id_x(), ncl = nclusters_x();
     v_begin = rank * a.N + static_cast<int>((static_cast<long long>(a.N) * cid) / ncl);
     v_end = rank * a.N + static_cast<int>((static_cast<long long>(a.N) * (cid + 1)) / ncl);
-  } else if constexpr (HALVES) {
-    h_begin = static_cast<int>((2ll * a.stages * blockIdx.x) / gridDim.x);
-    h_end = static_cast<int>((2ll * a.stages * (blockIdx.x + 1)) / gridDim.x);
-    v_begin = h_begin >> 1;
-    v_end = (h_end + 1) >> 1;
   } else {
     v_begin = static_cast<int>((static_cast<long long>(a.stages) * blockIdx.x) / gridDim.x);
     v_end = static_cast<int>((static_cast<long long>(a.stages) * (blockIdx.x + 1)) / gridDim.x);
@@ -301,12 +232,6 @@ __global__ void __launch_bounds__(StackGeom<S, kMixStack<T>>::THREADS, StackGeom
   for (int v = v_begin, it = 0; v < v_end; ++v, ++it) {
     const int s = it & 1;
     const int k = stage_of(v, a);
-    // HALVES: -1 = the whole stage; 0 / 1 = only rows [half * S/2, half * S/2 + S/2)
-    int half = -1;
-    if constexpr (HALVES) {
-      const int lo = max(2 * v, h_begin), hi = min(2 * v + 2, h_end);
-      if (hi - lo == 1) half = lo & 1;
-    }
     if (tid == 0 && v + 1 < v_end) {
       if (!MIX) bulk_wait_read_all();  // raw[s^1] carried the previous stage's output
       issue(stage_of(v + 1, a), s ^ 1);
@@ -421,31 +346,44 @@ __global__ void __launch_bounds__(StackGeom<S, kMixStack<T>>::THREADS, StackGeom
 #pragma unroll
       for (int o = 0; o < S; ++o) acc[r][o] = 0.f;
 
-    bool staged = false;  // a lone half stage stages its row right here
     if constexpr (MIX) {
-      if (HALVES && half >= 0) {
-        // One row per warp: row half * S/2 + rg.  out[s] was last read by
-        // the bulk store of stage it - 2, finished before the barrier that
-        // ended iteration it - 1.
-        float acc1[1][S];
+      const unsigned short* r16 = reinterpret_cast<const unsigned short*>(rs);
 #pragma unroll
-        for (int o = 0; o < S; ++o) acc1[0][o] = 0.f;
-        const int oy = half * (S / 2) + rg;
-        mix_rows<T, NHWC, S, 1, LANES>(rs, ln, oy, wh, acc1);
-        T* os1 = outb(s);
+      for (int ir = 0; ir < R + 6; ++ir) {
+        const int iy = rg * R + ir - kHalo;
+        if (iy < 0 || iy >= S) continue;  // zero-padding row (warp-uniform)
+        unsigned short xv[S];           // row iy of plane / channel ln
+        if constexpr (NHWC) {
 #pragma unroll
-        for (int o = 0; o < S; ++o) {
-          float val = acc1[0][o];
-          if (bbase != nullptr) val += bias;
-          const T e = from_acc<T>(val);
-          if (NHWC)
-            os1[(oy * S + o) * LANES + ln] = e;
-          else
-            os1[ln * PLANE + oy * S + o] = e;
+          for (int xx = 0; xx < S; ++xx) xv[xx] = r16[(iy * S + xx) * LANES + ln];
+        } else if constexpr (S % 2 == 0) {
+          const uint32_t* p = reinterpret_cast<const uint32_t*>(r16 + ln * PLANE + iy * S);
+#pragma unroll
+          for (int q2 = 0; q2 < S / 2; ++q2) {
+            const uint32_t u = p[q2];
+            xv[2 * q2] = half_of(u, 0);
+            xv[2 * q2 + 1] = half_of(u, 1);
+          }
+        } else {  // odd-width rows are not word aligned
+#pragma unroll
+          for (int xx = 0; xx < S; ++xx) xv[xx] = r16[ln * PLANE + iy * S + xx];
         }
-        staged = true;
-      } else {
-        mix_rows<T, NHWC, S, R, LANES>(rs, ln, rg * R, wh, acc);
+#pragma unroll
+        for (int kx = 0; kx < 7; ++kx) {
+#pragma unroll
+          for (int r = 0; r < R; ++r) {
+            const int ky = ir - r;
+            if (ky < 0 || ky >= 7) continue;
+            const int k = ky * 7 + kx;
+            const unsigned short wv = half_of(wh[k >> 1], k & 1);
+#pragma unroll
+            for (int o = 0; o < S; ++o) {
+              const int ix = o + kx - kHalo;
+              if (ix < 0 || ix >= S) continue;  // zero-padding column (compile time)
+              acc[r][o] = fma_mix(T(), xv[ix], wv, acc[r][o]);
+            }
+          }
+        }
       }
     } else {
       const float4* F4 = reinterpret_cast<const float4*>(F) + ln;
@@ -490,7 +428,7 @@ __global__ void __launch_bounds__(StackGeom<S, kMixStack<T>>::THREADS, StackGeom
 #pragma unroll
     for (int r = 0; r < R; ++r) {
       const int oy = rg * R + r;
-      if (oy >= S || staged) continue;
+      if (oy >= S) continue;
 #pragma unroll
       for (int o = 0; o < S; ++o) {
         float val = acc[r][o];
@@ -548,36 +486,7 @@ __global__ void __launch_bounds__(StackGeom<S, kMixStack<T>>::THREADS, StackGeom
     if (partial) {
       const long long base = static_cast<long long>(k) * LANES * PLANE;
       const long long left = (a.planes - static_cast<long long>(k) * LANES) * PLANE;
-      for (int i = tid; i < LANES * PLANE && i < left; i += G::THREADS)
-        if (half < 0 || (i % PLANE) / S / (S / 2) == half) y[base + i] = os[i];
-    } else if (HALVES && half >= 0) {
-      // A lone half stage: its rows are not a bulk-copy or TMA-box shaped
-      // region of the output, so the CTA copies them out with plain 32-bit
-      // stores (two 16-bit elements per word; rows of even width).
-      constexpr int HROWS = S / 2;
-      const uint32_t* o32 = reinterpret_cast<const uint32_t*>(os);
-      if constexpr (NHWC) {
-        // pixels [half * HROWS * S, +HROWS * S) x the group's channels
-        const int cg = k - n_img * a.cgroups;
-        const int nch = min(LANES, a.C - cg * LANES);  // even: C * 2 bytes is a multiple of 16
-        const int wpp = nch / 2;                       // words per pixel
-        const int pix0 = half * HROWS * S;
-        uint32_t* y32 = reinterpret_cast<uint32_t*>(
-            y + (static_cast<long long>(n_img) * PLANE + pix0) * a.C + cg * LANES);
-        for (int i = tid; i < HROWS * S * wpp; i += G::THREADS) {
-          const int px = i / wpp, wd = i - px * wpp;
-          y32[(static_cast<long long>(px) * a.C) / 2 + wd] = o32[((pix0 + px) * LANES) / 2 + wd];
-        }
-      } else {
-        // each plane's half is HROWS * S contiguous elements
-        constexpr int WPP = HROWS * S / 2;  // words per plane
-        uint32_t* y32 = reinterpret_cast<uint32_t*>(y + static_cast<long long>(k) * LANES * PLANE +
-                                                    half * HROWS * S);
-        for (int i = tid; i < LANES * WPP; i += G::THREADS) {
-          const int pl = i / WPP, wd = i - pl * WPP;
-          y32[pl * (PLANE / 2) + wd] = o32[(pl * PLANE + half * HROWS * S) / 2 + wd];
-        }
-      }
+      for (int i = tid; i < LANES * PLANE && i < left; i += G::THREADS) y[base + i] = os[i];
     } else if (tid == 0) {
       if (NHWC) {
         const int cg = k - n_img * a.cgroups;

@@ -147,9 +147,10 @@ __global__ void __launch_bounds__(kTileThreads, HOST_TAPS ? 5 : 4)
     fence_mbar_init();
   }
   __syncthreads();
-  // Launched with programmatic dependent launch: everything above overlaps
-  // the previous kernel's drain; every global read or write below comes
-  // after that kernel has completed and flushed (a no-op otherwise).
+  // Static-striding launches use programmatic dependent launch: everything
+  // above overlaps the previous kernel's drain; every global read or write
+  // below comes after that kernel has completed and flushed (a no-op for a
+  // launch without the attribute).
   grid_dependency_wait();
 
   const int total = a.total_tiles;
@@ -227,7 +228,6 @@ __global__ void __launch_bounds__(kTileThreads, HOST_TAPS ? 5 : 4)
           claim();
         } else {
           claiming = false;
-          launch_dependents();  // this CTA is on its last tile
         }
         next_tile[it & 1] = nt;  // read by every thread after this iteration's barrier
       }
@@ -236,7 +236,9 @@ __global__ void __launch_bounds__(kTileThreads, HOST_TAPS ? 5 : 4)
       // thread left that stage at the barrier that ended iteration it - 1.
       issue(t + (NS - 1) * stride, (it + NS - 1) % NS);
     } else if (tid == 0) {
-      launch_dependents();  // this CTA is on its last tile
+      // Static striding, last tile of this CTA: a kernel launched after this
+      // one with programmatic dependent launch may start its CTAs now.
+      launch_dependents();
     }
 
     const int q = fdiv(t, a.div_tx);

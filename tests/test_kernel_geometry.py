@@ -214,55 +214,3 @@ def test_restated_constants_match_the_kernel_sources():
               (int(capi["kShortR"]), int(capi["kNarrowLX"]))}
     assert shapes == {(8, 32), (7, 16), (2, 16)}
 
-
-def test_stack_half_units_cover_every_stage_row_once():
-    """Half-stage units of the 16-bit 14 x 14 / 28 x 28 stack kernel: the CTAs'
-    contiguous ranges of half units (rows [0, S/2) or [S/2, S) of a stage)
-    cover each stage's rows exactly once, a stage is computed whole when both
-    halves fall in one range, and the lone-half stores write each output
-    element of that half exactly once (NCHW: 32-bit words of a plane's
-    contiguous half; NHWC: 32-bit channel pairs of each pixel of the half)."""
-    for stages, grid in ((1536, 444), (3072, 444), (1536, 148), (7, 444), (384, 444), (1, 1), (5, 3)):
-        units = 2 * stages
-        grid = min(grid, units)
-        rows = {}
-        for b in range(grid):
-            h0, h1 = (units * b) // grid, (units * (b + 1)) // grid
-            assert h1 > h0
-            for v in range(h0 >> 1, (h1 + 1) >> 1):
-                lo, hi = max(2 * v, h0), min(2 * v + 2, h1)
-                halves = (0, 1) if hi - lo == 2 else (lo & 1,)
-                for hf in halves:
-                    assert (v, hf) not in rows
-                    rows[(v, hf)] = b
-        assert len(rows) == units
-    lanes = 32
-    for s in (14, 28):
-        hrows, plane = s // 2, s * s
-        for half in (0, 1):
-            # NCHW: words of each plane's half, read from the stage's [plane][row][col] buffer
-            wpp = hrows * s // 2
-            written = set()
-            for i in range(lanes * wpp):
-                pl, wd = divmod(i, wpp)
-                dst = pl * (plane // 2) + (half * hrows * s) // 2 + wd
-                src = (pl * plane + half * hrows * s) // 2 + wd
-                assert src == dst  # same [plane][row][col] layout on both sides
-                written.add(dst)
-            want = {(pl * plane + half * hrows * s) // 2 + w for pl in range(lanes) for w in range(wpp)}
-            assert written == want and len(written) == lanes * wpp
-            # NHWC, C channels, group cg: pixel-major, channel pairs
-            for C, cg in ((64, 1), (40, 1), (384, 3)):
-                nch = min(lanes, C - cg * lanes)
-                wpx = nch // 2
-                pix0 = half * hrows * s
-                got = set()
-                for i in range(hrows * s * wpx):
-                    px, wd = divmod(i, wpx)
-                    el = (pix0 + px) * C + cg * lanes + 2 * wd  # element offset in the image
-                    assert (px * C) % 2 == 0 and el % 2 == 0
-                    got.add(el)
-                    src_el = (pix0 + px) * lanes + 2 * wd      # stage buffer [pixel][lane]
-                    assert src_el % 2 == 0 and 2 * wd < nch
-                exp = {(pix0 + px) * C + cg * lanes + c for px in range(hrows * s) for c in range(0, nch, 2)}
-                assert got == exp
