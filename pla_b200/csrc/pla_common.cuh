@@ -175,6 +175,33 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
 }
 
 // ---------------------------------------------------------------------------
+// Cluster launch control (sm_100): a running CTA takes over the work of a CTA
+// of the same grid that has not started yet.  clc_try_cancel asks for one
+// (the 16-byte response lands in `resp`, 16-byte aligned shared memory, and
+// completes `bar`); clc_claimed_x reads the response after that phase: the
+// cancelled CTA's blockIdx.x, or -1 when no CTA was left to cancel.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void clc_try_cancel(void* resp, uint64_t* bar) {
+  mbar_arrive_expect_tx(bar, 16);
+  asm volatile("clusterlaunchcontrol.try_cancel.async.shared::cta.mbarrier::complete_tx::bytes.b128 [%0], [%1];"
+               ::"r"(smem_u32(resp)), "r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ int clc_claimed_x(const void* resp) {
+  int ok = 0, x = -1;
+  asm volatile(
+      "{ .reg .b128 r; .reg .pred p; ld.shared.b128 r, [%2];\n"
+      " clusterlaunchcontrol.query_cancel.is_canceled.pred.b128 p, r;\n"
+      " selp.s32 %0, 1, 0, p;\n"
+      " @p clusterlaunchcontrol.query_cancel.get_first_ctaid::x.b32.b128 %1, r; }"
+      : "=r"(ok), "+r"(x)
+      : "r"(smem_u32(resp))
+      : "memory");
+  return ok ? x : -1;
+}
+
+// ---------------------------------------------------------------------------
 // System-scope flags between GPUs (row-band halo exchange over peer memory).
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ unsigned int ld_acquire_sys(const unsigned int* p) {

@@ -159,12 +159,7 @@ __global__ void __launch_bounds__(kTileThreads, HOST_TAPS ? 5 : 4)
   bool claiming = dyn;
   // Thread 0: ask for the tile of a CTA that has not started yet; the
   // response (16 bytes) lands in claim_resp and completes claim_bar.
-  auto claim = [&]() {
-    mbar_arrive_expect_tx(claim_bar, 16);
-    asm volatile("clusterlaunchcontrol.try_cancel.async.shared::cta.mbarrier::complete_tx::bytes.b128 [%0], [%1];"
-                 ::"r"(smem_u32(claim_resp)), "r"(smem_u32(claim_bar))
-                 : "memory");
-  };
+  auto claim = [&]() { clc_try_cancel(claim_resp, claim_bar); };
 
   auto issue = [&](int tile, int stage) {
     const int q = fdiv(tile, a.div_tx);
@@ -211,18 +206,7 @@ __global__ void __launch_bounds__(kTileThreads, HOST_TAPS ? 5 : 4)
       // failed one.
       if (tid == 0) {
         int nt = -1;
-        if (claiming && mbar_wait_bounded(claim_bar, it & 1)) {
-          int ok = 0;
-          asm volatile(
-              "{ .reg .b128 r; .reg .pred p; ld.shared.b128 r, [%2];\n"
-              " clusterlaunchcontrol.query_cancel.is_canceled.pred.b128 p, r;\n"
-              " selp.s32 %0, 1, 0, p;\n"
-              " @p clusterlaunchcontrol.query_cancel.get_first_ctaid::x.b32.b128 %1, r; }"
-              : "=r"(ok), "+r"(nt)
-              : "r"(smem_u32(claim_resp))
-              : "memory");
-          if (!ok) nt = -1;
-        }
+        if (claiming && mbar_wait_bounded(claim_bar, it & 1)) nt = clc_claimed_x(claim_resp);
         if (nt >= 0) {
           issue(nt, stage ^ 1);
           claim();
