@@ -153,7 +153,7 @@ def test_against_reference_v2_fp16(H, W):
 
 
 # ---------------------------------------------------------------------------
-# the reference's CUTLASS depthwise kernels (K1-K6 of the survey):
+# the reference's CUTLASS depthwise kernels (its generated fp16 Toeplitz-GEMM variants):
 # data/depthwise_conv_7x7_cuda/model_cutlass.py (v1), model_cutlass_autotune_v5.py,
 # model_cutlass_autotune_v6.py, launch_depthwise_7x7_cutlass(x, packed_w, y,
 # n, c, h, w, fp16, stream); CUDA source strings compiled unmodified for
