@@ -87,6 +87,9 @@ __global__ void __launch_bounds__(PairGeom<T>::THREADS, 4)
     fence_mbar_init();
   }
   __syncthreads();
+  // Programmatic dependent launch: the set-up above overlaps the previous
+  // kernel's drain; every global access below comes after it completed.
+  grid_dependency_wait();
 
   const int v_begin = static_cast<int>((static_cast<long long>(a.stages) * blockIdx.x) / gridDim.x);
   const int v_end = static_cast<int>((static_cast<long long>(a.stages) * (blockIdx.x + 1)) / gridDim.x);
@@ -111,6 +114,7 @@ __global__ void __launch_bounds__(PairGeom<T>::THREADS, 4)
     // Slot s ^ 1 was last read in iteration it - 1, which every thread left
     // through the barrier that ended it.
     if (tid == 0 && v + 1 < v_end) issue(v + 1, s ^ 1);
+    if (tid == 0 && v + 1 == v_end) launch_dependents();  // last load issued
 
     const int p = pair_first_plane(v, a) + pl;
     const bool ok = p < a.planes;

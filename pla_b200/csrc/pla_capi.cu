@@ -396,7 +396,7 @@ int launch_pair(const void* x, const void* w, const void* b, void* y, int dtype,
   if (st != PLA_OK) return st;
   const long long slots = static_cast<long long>(d->sms) * per_sm;
   const int grid = static_cast<int>(a.stages < slots ? a.stages : slots);
-  pair_kernel<T><<<grid, G::THREADS, G::SMEM, stream>>>(map, a);
+  PLA_CUDA(launch_pdl(pair_kernel<T>, grid, G::THREADS, G::SMEM, stream, map, a));
   PLA_CUDA(cudaGetLastError());
   return PLA_OK;
 }
@@ -624,7 +624,7 @@ int launch_stack(const void* x, const void* w, const void* b, void* y, int dtype
   if (st != PLA_OK) return st;
   const long long slots = static_cast<long long>(d->sms) * per_sm;
   const int grid = static_cast<int>(stages < slots ? stages : slots);
-  stack_kernel<T, NHWC, S><<<grid, G::THREADS, M::TOTAL, stream>>>(xmap, ymap, a);
+  PLA_CUDA(launch_pdl(stack_kernel<T, NHWC, S>, grid, G::THREADS, M::TOTAL, stream, xmap, ymap, a));
   PLA_CUDA(cudaGetLastError());
   return PLA_OK;
 }

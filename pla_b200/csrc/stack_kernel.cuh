@@ -177,6 +177,10 @@ __global__ void __launch_bounds__(StackGeom<S, kMixStack<T>>::THREADS, StackGeom
     fence_mbar_init();
   }
   __syncthreads();
+  // Programmatic dependent launch (no-op without the launch attribute): the
+  // set-up above overlaps the previous kernel's drain; every global access
+  // below comes after that kernel completed.
+  grid_dependency_wait();
 
   const T* x = static_cast<const T*>(a.x);
   T* y = static_cast<T*>(a.y);
@@ -236,6 +240,7 @@ __global__ void __launch_bounds__(StackGeom<S, kMixStack<T>>::THREADS, StackGeom
       if (!MIX) bulk_wait_read_all();  // raw[s^1] carried the previous stage's output
       issue(stage_of(v + 1, a), s ^ 1);
     }
+    if (!LN && tid == 0 && v + 1 == v_end) launch_dependents();  // last load issued
 
     // ---- this lane's channel and filter --------------------------------
     int c;
