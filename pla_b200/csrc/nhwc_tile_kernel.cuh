@@ -93,6 +93,10 @@ __global__ void __launch_bounds__(NhwcTileGeom::THREADS, sizeof(T) == 2 ? 2 : 1)
     fence_mbar_init();
   }
   __syncthreads();
+  // Programmatic dependent launch (no-op without the launch attribute): the
+  // set-up above overlaps the previous kernel's drain; every global access
+  // below comes after that kernel completed.
+  grid_dependency_wait();
 
   // Stage v -> (channel group, image, tile); channel-group-major order.
   auto decode = [&](int v, int& cg, int& n, int& tx, int& ty) {
@@ -145,6 +149,7 @@ __global__ void __launch_bounds__(NhwcTileGeom::THREADS, sizeof(T) == 2 ? 2 : 1)
   for (int v = v_begin, it = 0; v < v_end; ++v, ++it) {
     const int s = it & 1;
     if (tid == 0 && v + 1 < v_end) issue(v + 1, s ^ 1);  // in[s ^ 1] was released by the last barrier
+    if (!LN && tid == 0 && v + 1 == v_end) launch_dependents();  // last load issued
 
     int cg, n, tx, ty;
     decode(v, cg, n, tx, ty);

@@ -673,7 +673,7 @@ int launch_nhwc_tile(const void* x, const void* w, const void* b, void* y, int d
   if (st != PLA_OK) return st;
   const long long slots = static_cast<long long>(d->sms) * per_sm;
   const int grid = static_cast<int>(a.stages < slots ? a.stages : slots);
-  nhwc_tile_kernel<T><<<grid, G::THREADS, M::TOTAL, stream>>>(xmap, ymap, a);
+  PLA_CUDA(launch_pdl(nhwc_tile_kernel<T>, grid, G::THREADS, M::TOTAL, stream, xmap, ymap, a));
   PLA_CUDA(cudaGetLastError());
   return PLA_OK;
 }
