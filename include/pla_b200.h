@@ -160,7 +160,10 @@ PLA_API int pla_depthwise_forward(const void* x, const void* w, const void* b, v
  * streams of the library (created once per device, on the first call made
  * with that device current), launches the problems round-robin and joins
  * back, so one problem's first tiles overlap another's last ones instead of
- * each launch paying its own ramp and drain.  Work queued on `stream` before
+ * each launch paying its own ramp and drain.  Problems are launched smallest
+ * first (by element count; ties in the given order): a large problem's
+ * persistent grid occupies every SM, so a small one queued behind it would
+ * start only in its drain.  Work queued on `stream` before
  * the call is finished before any problem starts; work queued after it
  * starts after every problem is done.  No problem's output may overlap any
  * problem's input or output (PLA_ERR_INVALID_ARGUMENT).  Arguments are
