@@ -50,6 +50,15 @@ import sys
 import threading
 import time
 
+# The reference arm times a CPU path with every host core.  torch.distributed.run
+# exports OMP_NUM_THREADS=1 to each rank, and the OpenMP runtime keeps the
+# value it read when torch loaded even after torch.set_num_threads(): the
+# convolution then ran 1.6x (one process) to 4x (under the launcher) slower.
+# Rank 0 of that arm is the only process that works, so it takes the cores
+# before torch is imported.
+if "--impl" in sys.argv and "reference" in sys.argv and os.environ.get("RANK", "0") == "0":
+    os.environ["OMP_NUM_THREADS"] = str(os.cpu_count() or 1)
+
 import numpy as np
 import torch
 import torch.distributed as dist
