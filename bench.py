@@ -900,7 +900,7 @@ def time_cpu_reference(wl, budget_s: float, steps: int | None = None, warmup: in
     total = sum(times)
     gbs = bytes_rows(rows) * len(times) / total / 1e9
     sample = f"{what}; {len(times)} calls of {rows} of {nrows} rows/images each, " \
-             f"{total:.2f} s, {threads} threads"
+             f"{total:.2f} s, {threads} threads (OMP_NUM_THREADS={os.environ.get('OMP_NUM_THREADS', 'unset')})"
     return gbs, {"value": gbs, "unit": "GB/s", "cores": torch.get_num_threads(),
                  "kind": getattr(wl, "cpu_kind", "reference"),
                  "sample": sample, "s_per_call": total / len(times)}

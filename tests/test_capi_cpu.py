@@ -191,6 +191,31 @@ def test_bench_reference_arm_line_on_cpu():
     assert d["config"]["workload"] == "depthwise7x7_cfg1_1x96x56x56_f32"
 
 
+def test_bench_reference_arm_under_torchrun_uses_every_core():
+    """Launched as the scaling run launches it (torch.distributed.run, 2 ranks,
+    which export OMP_NUM_THREADS=1): rank 0 alone prints the line, timed with
+    every host core; the other rank exits 0 without work."""
+    import json
+    import socket
+    import subprocess
+    import sys
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    r = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
+                        "--master-addr", "127.0.0.1", "--master-port", str(port), os.path.join(ROOT, "bench.py"),
+                        "--impl", "reference", "--gpus", "2", "--steps", "2", "--warmup", "1", "--workload", "dw_cfg1"],
+                       capture_output=True, text=True, timeout=600, cwd=ROOT)
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = [ln for ln in r.stdout.splitlines() if ln.startswith("{")]
+    assert len(lines) == 1
+    d = json.loads(lines[0])
+    assert d["impl"] == "reference" and d["n_gpus"] == 2
+    assert d["cpu_baseline"]["cores"] == (os.cpu_count() or 1)
+    assert f"{os.cpu_count() or 1} threads (OMP_NUM_THREADS={os.cpu_count() or 1})" in d["cpu_baseline"]["sample"]
+
+
 def _bench_module():
     import importlib.util
 
