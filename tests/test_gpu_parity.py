@@ -231,6 +231,41 @@ def test_stencil_cfg2_full_size():
     torch.testing.assert_close(y.cpu(), ref, rtol=1e-5, atol=1e-5)
 
 
+def test_host_taps_tile_claiming_ragged_planes():
+    """Large single fp32 planes with host taps: tens of thousands of 32 x 128
+    tiles, so the tile kernel claims the tiles of CTAs not yet started
+    (launch control).  The shapes end in a partial tile column (W % 128 != 0)
+    and a partial tile row, carry a bias, and include band steps over
+    sub-ranges of a band buffer with its 3 halo rows, which must stay
+    untouched."""
+    from pla_b200 import _lib, stencil7x7
+
+    g = torch.Generator().manual_seed(31)
+    H, W = 4001, 40004
+    x = torch.rand(1, 1, H, W, generator=g) * 2 - 1
+    w = (torch.rand(1, 1, 7, 7, generator=g) * 2 - 1) / 49
+    b = (torch.rand(1, generator=g) * 2 - 1) / 49
+    xd, wd, bd = x.to(DEV), w.to(DEV), b.to(DEV)
+    y = stencil7x7(xd, wd, bd, host_taps=_lib.HostTaps().update(wd, bd))
+    _assert_equal(y, oracle.stencil7x7(x, w, b))
+
+    rows, W2 = 8000, 20000
+    grid = torch.rand(rows + 6, W2, generator=g) * 2 - 1
+    src = grid.to(DEV)
+    taps, hb = _lib.HostTaps().update(wd, None).args()
+    L = _lib.lib()
+    for r_a, r_b in [(0, rows), (3, rows - 3), (1000, 1005 + 218 * 30)]:
+        dst = torch.full((rows + 6, W2), 7.0, device=DEV)
+        st = L.pla_stencil7x7_band_step_taps(src.data_ptr(), taps, hb, dst.data_ptr(), rows, W2, r_a, r_b, 1,
+                                             torch.cuda.current_stream().cuda_stream)
+        assert st == 0
+        out = dst.cpu()
+        # band row r reads buffer rows r .. r + 6 (band rows r - 3 .. r + 3)
+        ref = oracle.stencil7x7_rows(grid, w.view(7, 7), r_a + 3, r_b + 3)
+        _assert_equal(out[3 + r_a:3 + r_b], ref)
+        assert torch.all(out[:3 + r_a] == 7.0) and torch.all(out[3 + r_b:] == 7.0)
+
+
 # --------------------------------------------------------------------------
 # iterated stencil
 # --------------------------------------------------------------------------
