@@ -168,6 +168,12 @@ PLA_API int pla_depthwise_forward(const void* x, const void* w, const void* b, v
  * starts after every problem is done.  No problem's output may overlap any
  * problem's input or output (PLA_ERR_INVALID_ARGUMENT).  Arguments are
  * checked for every problem before anything is launched.
+ *
+ * The library streams are shared by every caller on the device: calls made
+ * on different streams are ordered after one another on them (correct, but
+ * not concurrent with each other), and a stream capture that contains a
+ * call holds them in capture mode until the capture ends, so while it is
+ * open no other thread may call this function on that device.
  */
 typedef struct pla_dw_problem {
   const void* x;
